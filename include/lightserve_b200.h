@@ -1,0 +1,149 @@
+/*
+ * lightserve_b200 — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Each entry point replaces one operator of lightserve's Python/Triton hot
+ * path (citations are file:line inside the lightserve project). The ABI takes
+ * only plain pointers, sizes, element strides (in elements, not bytes), a
+ * dtype code and a cudaStream_t passed as void*. It never allocates device
+ * memory and never synchronises: callers own every buffer, including the
+ * scratch ("workspace") buffers whose sizes the *_workspace_size helpers
+ * report. All launches are recorded on `stream` and can be captured into a
+ * CUDA graph.
+ *
+ * Return value: LSB_OK (0) on success, otherwise an LSB_ERR_* code; the
+ * reason is available from lsb_last_error() on the calling thread.
+ */
+#ifndef LIGHTSERVE_B200_H_
+#define LIGHTSERVE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LSB_API __attribute__((visibility("default")))
+#else
+#define LSB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ----------------------------------------------------------------- codes -- */
+#define LSB_OK 0
+#define LSB_ERR_INVALID 1     /* bad shape, stride, pointer or size        */
+#define LSB_ERR_UNSUPPORTED 2 /* valid request this build cannot serve     */
+#define LSB_ERR_CUDA 3        /* a CUDA runtime call or launch failed      */
+
+#define LSB_DTYPE_F32 0
+#define LSB_DTYPE_BF16 1
+#define LSB_DTYPE_F16 2
+
+/* Attention forward implementation selector (lsb_attn_fwd `impl`). */
+#define LSB_IMPL_AUTO 0    /* tcgen05 kernel when eligible, else SIMT kernel */
+#define LSB_IMPL_SIMT 1    /* CUDA-core kernel, any dtype / head dim <= 256  */
+#define LSB_IMPL_TCGEN05 2 /* tcgen05 + TMEM + TMA kernel; error if ineligible */
+
+/* Message describing the last failure on this thread ("" if none). */
+LSB_API const char* lsb_last_error(void);
+
+/* Library version string. */
+LSB_API const char* lsb_version(void);
+
+/*
+ * Fused residual-add + RMSNorm.
+ * Replaces fused_add_rmsnorm / _fused_add_rmsnorm_kernel
+ * (kernels/fused_rmsnorm_residual.py:73-117, :31-70):
+ *   h   = x + residual                       (stored in the input dtype)
+ *   out = (float(h) * rsqrt(mean(float(h)^2) + eps) * float(w)) -> dtype
+ * x, residual, out, h are [M, N] row-major with row strides ld_*; w is [N].
+ */
+LSB_API int lsb_rmsnorm_residual(const void* x, const void* residual, const void* weight,
+                         void* out, void* h_out, int64_t M, int64_t N,
+                         int64_t ld_x, int64_t ld_r, int64_t ld_out, int64_t ld_h,
+                         float eps, int dtype, void* stream);
+
+/*
+ * FlashAttention forward, O = softmax(Q K^T * scale [+ causal mask]) V.
+ * Replaces flash_attention_forward / _flash_attn_fwd_kernel
+ * (kernels/flash_attention.py:182-222, :84-179) and, when lse != NULL,
+ * _flash_attention_forward_lse / _flash_attn_fwd_lse_kernel
+ * (kernels/flash_attention_backward.py:172-199, :88-169).
+ * q, k, v, o: [B, H, N, D] with element strides s*[4] = {b, h, n, d}.
+ * lse (optional): fp32 [B, H, N] contiguous, lse = rowmax + ln(rowsum(exp)).
+ */
+LSB_API int lsb_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                 int64_t B, int64_t H, int64_t N, int64_t D,
+                 const int64_t* sq, const int64_t* sk, const int64_t* sv,
+                 const int64_t* so, float scale, int causal, int dtype, int impl,
+                 void* stream);
+
+/* Bytes of fp32 scratch lsb_attn_bwd needs: Dsum [B,H,N] + dQ accumulator
+ * [B,H,N,D] (each region 256-byte aligned). */
+LSB_API int64_t lsb_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D);
+
+/*
+ * FlashAttention backward (recomputation strategy).
+ * Replaces _flash_attention_backward and its two kernels
+ * (kernels/flash_attention_backward.py:333-382, :202-229, :232-330):
+ *   Dsum = rowsum(dO * O); P = exp(S - lse); dV = P^T dO; dP = dO V^T;
+ *   dS = P * (dP - Dsum); dK = dS^T Q * scale; dQ = dS K * scale.
+ * Strides are element strides {b, h, n, d} for q,k,v,o,do,dq,dk,dv.
+ * workspace: >= lsb_attn_bwd_workspace_size bytes, 256-byte aligned.
+ */
+LSB_API int lsb_attn_bwd(const void* q, const void* k, const void* v, const void* o,
+                 const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                 int64_t B, int64_t H, int64_t N, int64_t D,
+                 const int64_t* sq, const int64_t* sk, const int64_t* sv,
+                 const int64_t* so, const int64_t* sdo, const int64_t* sdq,
+                 const int64_t* sdk, const int64_t* sdv, float scale, int causal,
+                 int dtype, int impl, void* workspace, int64_t workspace_bytes,
+                 void* stream);
+
+/*
+ * Write new K/V rows into the paged KV cache.
+ * No counterpart kernel exists in lightserve (engine/README.md:142-155 says
+ * the decode path is missing); the slot arithmetic follows the block-table
+ * convention of engine/block_manager.py:58-61 (block i of a request holds
+ * tokens [i*block_size, (i+1)*block_size)).
+ * k, v: [T, H, D] (strides {t, h} in elements, d contiguous).
+ * k_cache, v_cache: [num_blocks, H, block_size, D] contiguous.
+ * slot_mapping: int64 [T], slot = block_id * block_size + offset; a negative
+ * slot skips that row.
+ */
+LSB_API int lsb_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache,
+                       const int64_t* slot_mapping, int64_t T, int64_t H, int64_t D,
+                       int64_t num_blocks, int64_t block_size,
+                       int64_t sk_t, int64_t sk_h, int64_t sv_t, int64_t sv_h,
+                       int dtype, void* stream);
+
+/* Bytes of fp32 scratch lsb_paged_decode needs for split-context partials. */
+LSB_API int64_t lsb_paged_decode_workspace_size(int64_t S, int64_t H, int64_t D,
+                                        int64_t max_blocks_per_seq,
+                                        int64_t block_size);
+
+/*
+ * Paged-KV decode attention (one query token per sequence).
+ * New operator: lightserve has no decode-shaped attention kernel
+ * (engine/README.md:142-147, engine/request.py:86-93); its oracle is the
+ * full-recompute decode of model/cuda_graph_decode.py:108-149 over
+ * model/minimal_llama.py:253-293.
+ * q, o: [S, H, D] (strides {s, h}, d contiguous).
+ * k_cache, v_cache: [num_blocks, H, block_size, D] contiguous.
+ * block_tables: int32 [S, max_blocks_per_seq] row-major; context_lens: int32 [S].
+ * o[s,h] = softmax(q[s,h] . K[s,h,:L]^T * scale) V[s,h,:L], L = context_lens[s].
+ * workspace: >= lsb_paged_decode_workspace_size bytes (may be NULL when that
+ * size is 0).
+ */
+LSB_API int lsb_paged_decode(const void* q, const void* k_cache, const void* v_cache,
+                     const int32_t* block_tables, const int32_t* context_lens,
+                     void* o, int64_t S, int64_t H, int64_t D,
+                     int64_t max_blocks_per_seq, int64_t block_size,
+                     int64_t num_blocks, int64_t sq_s, int64_t sq_h,
+                     int64_t so_s, int64_t so_h, float scale, int dtype,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIGHTSERVE_B200_H_ */

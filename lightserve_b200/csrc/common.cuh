@@ -1,0 +1,144 @@
+// Shared helpers for the lightserve_b200 CUDA kernels (sm_100a only).
+//
+// Every kernel in this library is launched through an `extern "C"` entry point
+// declared in include/lightserve_b200.h. Entry points never allocate device
+// memory and never synchronise the stream, so every one of them can be
+// recorded into a CUDA graph. Errors are reported as an int status plus a
+// thread-local message readable through lsb_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+#include "../../include/lightserve_b200.h"
+
+namespace lsb {
+
+// ---------------------------------------------------------------- errors ---
+
+void set_error(const char* fmt, ...);
+
+#define LSB_CHECK_ARG(cond, ...)                                   \
+  do {                                                             \
+    if (!(cond)) {                                                 \
+      ::lsb::set_error(__VA_ARGS__);                               \
+      return LSB_ERR_INVALID;                                      \
+    }                                                              \
+  } while (0)
+
+#define LSB_CHECK_LAUNCH(what)                                                    \
+  do {                                                                            \
+    cudaError_t _e = cudaGetLastError();                                          \
+    if (_e != cudaSuccess) {                                                      \
+      ::lsb::set_error("%s: CUDA launch failed: %s", what, cudaGetErrorString(_e)); \
+      return LSB_ERR_CUDA;                                                        \
+    }                                                                             \
+  } while (0)
+
+#define LSB_CUDA_OK(call, what)                                                   \
+  do {                                                                            \
+    cudaError_t _e = (call);                                                      \
+    if (_e != cudaSuccess) {                                                      \
+      ::lsb::set_error("%s: %s", what, cudaGetErrorString(_e));                   \
+      return LSB_ERR_CUDA;                                                        \
+    }                                                                             \
+  } while (0)
+
+inline int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// ----------------------------------------------------------- dtype traits ---
+
+template <typename T> struct Dt;
+template <> struct Dt<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Dt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+template <> struct Dt<__half> {
+  static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T x) { return Dt<T>::to_f(x); }
+template <typename T> __device__ __forceinline__ T from_f(float x) { return Dt<T>::from_f(x); }
+
+inline int dtype_size(int dtype) {
+  switch (dtype) {
+    case LSB_DTYPE_F32: return 4;
+    case LSB_DTYPE_BF16: return 2;
+    case LSB_DTYPE_F16: return 2;
+    default: return 0;
+  }
+}
+
+// Dispatch a templated body over the three element types.
+#define LSB_DISPATCH_DTYPE(dtype, T, ...)                 \
+  [&]() -> int {                                          \
+    switch (dtype) {                                      \
+      case LSB_DTYPE_F32: { using T = float; return __VA_ARGS__(); }          \
+      case LSB_DTYPE_BF16: { using T = __nv_bfloat16; return __VA_ARGS__(); } \
+      case LSB_DTYPE_F16: { using T = __half; return __VA_ARGS__(); }         \
+      default: ::lsb::set_error("unsupported dtype code %d", (int)dtype); return LSB_ERR_UNSUPPORTED; \
+    }                                                     \
+  }()
+
+// 16-byte vector of T.
+template <typename T>
+struct alignas(16) Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_vec16(const T* p) {
+  Vec16<T> r;
+  *reinterpret_cast<uint4*>(&r) = *reinterpret_cast<const uint4*>(p);
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_vec16_stream(const T* p) {
+  // Streaming load: data read once, do not keep in L1.
+  Vec16<T> r;
+  *reinterpret_cast<uint4*>(&r) = __ldcs(reinterpret_cast<const uint4*>(p));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_vec16(T* p, const Vec16<T>& v) {
+  *reinterpret_cast<uint4*>(p) = *reinterpret_cast<const uint4*>(&v);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace lsb

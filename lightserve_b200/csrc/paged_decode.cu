@@ -1,0 +1,365 @@
+// Paged-KV decode attention and the KV-cache write (HBM-bound).
+//
+// lightserve has no decode-shaped attention kernel (engine/README.md:142-147);
+// its decode re-runs the full causal forward every step
+// (model/cuda_graph_decode.py:108-149). These kernels compute the same
+// attention row -- the newest position attending to every cached position
+// 0..L-1 of its own sequence, which is the last row of the causal mask -- from
+// a paged cache addressed through engine/block_manager.py's block tables
+// (block i of a request holds tokens [i*block_size, (i+1)*block_size),
+// engine/block_manager.py:58-61).
+//
+// Cache layout: [num_blocks, H, block_size, D] per layer, so one (block, head)
+// is a contiguous block_size*D run (4 KiB for bf16, 16 x 128): each half-warp
+// reads a whole 256-byte token row with 16-byte loads.
+//
+// Decode kernel (flash-decoding): grid (partition, head, sequence). Each CTA
+// covers PART_TOKENS cached tokens of one (sequence, head); its 4 warps take
+// interleaved rounds of 16 tokens, issue all K and V loads of a round before
+// any math (16 x 16 B in flight per lane), and keep an online softmax in fp32
+// with exp2 on log2(e)-prescaled scores. Sequences with one partition write
+// the output directly; longer ones write (m, l, acc) partials to the
+// caller-provided workspace and a combine kernel merges them.
+#include "common.cuh"
+
+#include <type_traits>
+
+namespace lsb {
+
+constexpr int PD_PART_TOKENS = 512;
+constexpr int PD_WARPS = 4;
+constexpr float PD_LOG2E = 1.4426950408889634f;
+
+static inline int64_t pd_max_parts(int64_t max_blocks, int64_t bs) {
+  const int64_t max_tokens = max_blocks * bs;
+  return (max_tokens + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
+}
+
+// Workspace: part_m [S*H*P], part_l [S*H*P], part_acc [S*H*P*D] (fp32).
+template <typename T, int D>
+__global__ void __launch_bounds__(PD_WARPS * 32)
+paged_decode_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
+                    const T* __restrict__ v_cache, const int32_t* __restrict__ block_tables,
+                    const int32_t* __restrict__ context_lens, T* __restrict__ o, int H,
+                    int max_blocks, int num_blocks, int bs_log2, int64_t sq_s, int64_t sq_h, int64_t so_s,
+                    int64_t so_h, float scale_log2, int max_parts, float* __restrict__ part_m,
+                    float* __restrict__ part_l, float* __restrict__ part_acc) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int LPT = D / VEC;         // lanes per token row
+  constexpr int TPW = 32 / LPT;        // token rows per warp-wide load
+  constexpr int U = (16 / TPW) > 0 ? (16 / TPW) : 1;  // loads per lane per round
+  constexpr int ROUND = TPW * U;       // tokens per warp round
+  static_assert(LPT >= 1 && LPT <= 32 && (32 % LPT) == 0, "unsupported head dim");
+
+  const int part = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  // Positions past the block table's capacity are never read.
+  const int ctx = max(0, min(context_lens[s], max_blocks << bs_log2));
+  const int t_begin = part * PD_PART_TOKENS;
+  if (t_begin >= ctx && !(ctx == 0 && part == 0)) return;
+  const int t_end = min(ctx, t_begin + PD_PART_TOKENS);
+  const int nparts = (ctx + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane / LPT;          // which token row of a load this lane reads
+  const int dofs = (lane % LPT) * VEC; // which 16-byte chunk of that row
+
+  float qf[VEC];
+  {
+    Vec16<T> qv = ld_vec16(q + s * sq_s + h * sq_h + dofs);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) qf[j] = to_f(qv.v[j]) * scale_log2;
+  }
+
+  const int32_t* bt = block_tables + (int64_t)s * max_blocks;
+  const int bs = 1 << bs_log2;
+  const int64_t head_stride = (int64_t)bs * D;        // elements between heads in a block
+  const int64_t block_stride = (int64_t)H * head_stride;
+
+  float m = -INFINITY, l = 0.f;
+  float acc[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+
+  for (int r0 = t_begin + warp * ROUND; r0 < t_end; r0 += PD_WARPS * ROUND) {
+    Vec16<T> kv[U], vv[U];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = r0 + u * TPW + grp;
+      ok[u] = t < t_end;
+      const int blk = ok[u] ? bt[t >> bs_log2] : 0;
+      ok[u] = ok[u] && blk >= 0 && blk < num_blocks;  // bad ids read nothing
+      if (ok[u]) {
+        const int64_t off = blk * block_stride + h * head_stride +
+                            (int64_t)(t & (bs - 1)) * D + dofs;
+        kv[u] = ld_vec16_stream(k_cache + off);
+        vv[u] = ld_vec16_stream(v_cache + off);
+      }
+    }
+    float sc[U];
+    float rmax = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float d = 0.f;
+      if (ok[u]) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) d = fmaf(qf[j], to_f(kv[u].v[j]), d);
+      }
+#pragma unroll
+      for (int off = LPT / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      sc[u] = ok[u] ? d : -INFINITY;
+      rmax = fmaxf(rmax, sc[u]);
+    }
+#pragma unroll
+    for (int off = 16; off >= LPT; off >>= 1)
+      rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+    const float m_new = fmaxf(m, rmax);  // finite: every round holds >= 1 valid token
+    const float alpha = exp2f(m - m_new);
+    l *= alpha;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] *= alpha;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float p = exp2f(sc[u] - m_new);  // 0 for masked rows
+      l += p;
+      if (ok[u]) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[j] = fmaf(p, to_f(vv[u].v[j]), acc[j]);
+      }
+    }
+    m = m_new;
+  }
+
+  // Merge token groups inside the warp (same d chunk, different rows).
+#pragma unroll
+  for (int off = 16; off >= LPT; off >>= 1) {
+    l += __shfl_xor_sync(0xffffffffu, l, off);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+  }
+
+  __shared__ float sm_m[PD_WARPS], sm_l[PD_WARPS];
+  __shared__ float sm_acc[PD_WARPS][D];
+  if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
+  if (grp == 0) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) sm_acc[warp][dofs + j] = acc[j];
+  }
+  __syncthreads();
+
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < PD_WARPS; ++w) M = fmaxf(M, sm_m[w]);
+  float wts[PD_WARPS];
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < PD_WARPS; ++w) {
+    wts[w] = (sm_m[w] == -INFINITY) ? 0.f : exp2f(sm_m[w] - M);
+    L += wts[w] * sm_l[w];
+  }
+
+  if (nparts <= 1) {
+    T* orow = o + s * so_s + h * so_h;
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < PD_WARPS; ++w) a = fmaf(wts[w], sm_acc[w][d], a);
+      orow[d] = from_f<T>(a * inv);
+    }
+  } else {
+    const int64_t pi = ((int64_t)s * H + h) * max_parts + part;
+    if (threadIdx.x == 0) { part_m[pi] = M; part_l[pi] = L; }
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < PD_WARPS; ++w) a = fmaf(wts[w], sm_acc[w][d], a);
+      part_acc[pi * D + d] = a;
+    }
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128)
+paged_decode_combine_kernel(const int32_t* __restrict__ context_lens, int max_tokens,
+                            T* __restrict__ o, int H, int64_t so_s, int64_t so_h, int max_parts,
+                            const float* __restrict__ part_m, const float* __restrict__ part_l,
+                            const float* __restrict__ part_acc) {
+  const int h = blockIdx.x, s = blockIdx.y;
+  const int ctx = max(0, min(context_lens[s], max_tokens));
+  const int nparts = (ctx + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
+  if (nparts <= 1) return;  // written directly by the decode kernel
+  const int64_t base = ((int64_t)s * H + h) * max_parts;
+  float M = -INFINITY;
+  for (int p = 0; p < nparts; ++p) M = fmaxf(M, part_m[base + p]);
+  float L = 0.f;
+  for (int p = 0; p < nparts; ++p) L += exp2f(part_m[base + p] - M) * part_l[base + p];
+  const float inv = 1.0f / L;
+  T* orow = o + s * so_s + h * so_h;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float a = 0.f;
+    for (int p = 0; p < nparts; ++p)
+      a = fmaf(exp2f(part_m[base + p] - M), part_acc[(base + p) * D + d], a);
+    orow[d] = from_f<T>(a * inv);
+  }
+}
+
+template <typename T, int D>
+static int launch_paged_decode(const void* q, const void* kc, const void* vc,
+                               const int32_t* bt, const int32_t* cl, void* o, int64_t S,
+                               int64_t H, int64_t max_blocks, int64_t num_blocks, int bs_log2, int64_t sq_s,
+                               int64_t sq_h, int64_t so_s, int64_t so_h, float scale,
+                               void* ws, int64_t ws_bytes, cudaStream_t st) {
+  const int64_t P = pd_max_parts(max_blocks, (int64_t)1 << bs_log2);
+  float* pm = nullptr; float* pl = nullptr; float* pa = nullptr;
+  if (P > 1) {
+    const int64_t need = lsb_paged_decode_workspace_size(S, H, D, max_blocks, (int64_t)1 << bs_log2);
+    LSB_CHECK_ARG(ws != nullptr && ws_bytes >= need,
+                  "paged_decode: workspace of %lld bytes required, got %lld", (long long)need,
+                  (long long)ws_bytes);
+    LSB_CHECK_ARG(aligned16(ws), "paged_decode: workspace must be 16-byte aligned");
+    pm = (float*)ws;
+    pl = pm + S * H * P;
+    pa = pl + S * H * P;
+  }
+  dim3 grid((unsigned)P, (unsigned)H, (unsigned)S);
+  paged_decode_kernel<T, D><<<grid, PD_WARPS * 32, 0, st>>>(
+      (const T*)q, (const T*)kc, (const T*)vc, bt, cl, (T*)o, (int)H, (int)max_blocks, (int)num_blocks, bs_log2,
+      sq_s, sq_h, so_s, so_h, scale * PD_LOG2E, (int)P, pm, pl, pa);
+  LSB_CHECK_LAUNCH("paged_decode");
+  if (P > 1) {
+    paged_decode_combine_kernel<T, D><<<dim3((unsigned)H, (unsigned)S), 128, 0, st>>>(
+        cl, (int)(max_blocks << bs_log2), (T*)o, (int)H, so_s, so_h, (int)P, pm, pl, pa);
+    LSB_CHECK_LAUNCH("paged_decode_combine");
+  }
+  return LSB_OK;
+}
+
+template <typename T>
+__global__ void kv_cache_write_kernel(const T* __restrict__ k, const T* __restrict__ v,
+                                      T* __restrict__ k_cache, T* __restrict__ v_cache,
+                                      const int64_t* __restrict__ slots, int64_t T_, int H, int D,
+                                      int bs, int64_t num_blocks_x_bs, int64_t sk_t, int64_t sk_h, int64_t sv_t,
+                                      int64_t sv_h, int vec) {
+  // One warp per (token, head) row.
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= T_ * H) return;
+  const int64_t t = row / H;
+  const int h = (int)(row % H);
+  const int64_t slot = slots[t];
+  if (slot < 0 || slot >= (int64_t)num_blocks_x_bs) return;
+  const int64_t blk = slot / bs, off = slot % bs;
+  const int64_t dst = ((blk * H + h) * bs + off) * D;
+  const T* ks = k + t * sk_t + h * sk_h;
+  const T* vs = v + t * sv_t + h * sv_h;
+  if (vec) {
+    constexpr int VEC = 16 / sizeof(T);
+    for (int d = lane * VEC; d < D; d += 32 * VEC) {
+      st_vec16(k_cache + dst + d, ld_vec16(ks + d));
+      st_vec16(v_cache + dst + d, ld_vec16(vs + d));
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      k_cache[dst + d] = ks[d];
+      v_cache[dst + d] = vs[d];
+    }
+  }
+}
+
+}  // namespace lsb
+
+extern "C" int64_t lsb_paged_decode_workspace_size(int64_t S, int64_t H, int64_t D,
+                                                   int64_t max_blocks_per_seq,
+                                                   int64_t block_size) {
+  if (S <= 0 || H <= 0 || D <= 0 || max_blocks_per_seq <= 0 || block_size <= 0) return 0;
+  const int64_t P = lsb::pd_max_parts(max_blocks_per_seq, block_size);
+  if (P <= 1) return 0;
+  return (int64_t)sizeof(float) * S * H * P * (D + 2);
+}
+
+extern "C" int lsb_paged_decode(const void* q, const void* k_cache, const void* v_cache,
+                                const int32_t* block_tables, const int32_t* context_lens,
+                                void* o, int64_t S, int64_t H, int64_t D,
+                                int64_t max_blocks_per_seq, int64_t block_size,
+                                int64_t num_blocks, int64_t sq_s, int64_t sq_h, int64_t so_s,
+                                int64_t so_h, float scale, int dtype, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  LSB_CHECK_ARG(S >= 0 && H > 0 && D > 0 && max_blocks_per_seq > 0 && num_blocks > 0,
+                "paged_decode: bad sizes S=%lld H=%lld D=%lld max_blocks=%lld num_blocks=%lld",
+                (long long)S, (long long)H, (long long)D, (long long)max_blocks_per_seq,
+                (long long)num_blocks);
+  LSB_CHECK_ARG(block_size > 0 && (block_size & (block_size - 1)) == 0,
+                "paged_decode: block_size %lld must be a power of two", (long long)block_size);
+  if (S == 0) return LSB_OK;
+  LSB_CHECK_ARG(q && k_cache && v_cache && block_tables && context_lens && o,
+                "paged_decode: null pointer");
+  const int esz = lsb::dtype_size(dtype);
+  LSB_CHECK_ARG(esz > 0, "paged_decode: unsupported dtype %d", dtype);
+  LSB_CHECK_ARG(lsb::aligned16(q) && lsb::aligned16(k_cache) && lsb::aligned16(v_cache),
+                "paged_decode: q and caches must be 16-byte aligned");
+  LSB_CHECK_ARG((sq_s * esz) % 16 == 0 && (sq_h * esz) % 16 == 0,
+                "paged_decode: q strides must be multiples of 16 bytes");
+  LSB_CHECK_ARG(S <= 65535 && H <= 65535, "paged_decode: S or H above 65535");
+  int bs_log2 = 0;
+  while ((1LL << bs_log2) < block_size) ++bs_log2;
+  cudaStream_t st = (cudaStream_t)stream;
+  auto go = [&](auto tag, auto dtag) -> int {
+    using T = decltype(tag);
+    constexpr int DD = decltype(dtag)::value;
+    return lsb::launch_paged_decode<T, DD>(q, k_cache, v_cache, block_tables, context_lens, o, S,
+                                           H, max_blocks_per_seq, num_blocks, bs_log2, sq_s, sq_h, so_s, so_h,
+                                           scale, workspace, workspace_bytes, st);
+  };
+  using I64 = std::integral_constant<int, 64>;
+  using I128 = std::integral_constant<int, 128>;
+  using I256 = std::integral_constant<int, 256>;
+  using I32 = std::integral_constant<int, 32>;
+  switch (dtype) {
+    case LSB_DTYPE_BF16:
+      if (D == 64) return go(__nv_bfloat16{}, I64{});
+      if (D == 128) return go(__nv_bfloat16{}, I128{});
+      if (D == 256) return go(__nv_bfloat16{}, I256{});
+      break;
+    case LSB_DTYPE_F16:
+      if (D == 64) return go(__half{}, I64{});
+      if (D == 128) return go(__half{}, I128{});
+      if (D == 256) return go(__half{}, I256{});
+      break;
+    case LSB_DTYPE_F32:
+      if (D == 32) return go(float{}, I32{});
+      if (D == 64) return go(float{}, I64{});
+      if (D == 128) return go(float{}, I128{});
+      break;
+  }
+  lsb::set_error("paged_decode: head dim %lld unsupported for dtype %d", (long long)D, dtype);
+  return LSB_ERR_UNSUPPORTED;
+}
+
+extern "C" int lsb_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache,
+                                  const int64_t* slot_mapping, int64_t T, int64_t H, int64_t D,
+                                  int64_t num_blocks, int64_t block_size, int64_t sk_t,
+                                  int64_t sk_h, int64_t sv_t, int64_t sv_h, int dtype,
+                                  void* stream) {
+  LSB_CHECK_ARG(T >= 0 && H > 0 && D > 0 && num_blocks > 0 && block_size > 0,
+                "kv_cache_write: bad sizes");
+  if (T == 0) return LSB_OK;
+  LSB_CHECK_ARG(k && v && k_cache && v_cache && slot_mapping, "kv_cache_write: null pointer");
+  const int esz = lsb::dtype_size(dtype);
+  LSB_CHECK_ARG(esz > 0, "kv_cache_write: unsupported dtype %d", dtype);
+  const bool vec = ((D * esz) % 16 == 0) && lsb::aligned16(k) && lsb::aligned16(v) &&
+                   lsb::aligned16(k_cache) && lsb::aligned16(v_cache) &&
+                   (sk_t * esz) % 16 == 0 && (sk_h * esz) % 16 == 0 && (sv_t * esz) % 16 == 0 &&
+                   (sv_h * esz) % 16 == 0;
+  const int64_t rows = T * H;
+  const int threads = 256;
+  const int64_t blocks = (rows * 32 + threads - 1) / threads;
+  cudaStream_t st = (cudaStream_t)stream;
+  return LSB_DISPATCH_DTYPE(dtype, Tt, [&] {
+    lsb::kv_cache_write_kernel<Tt><<<(unsigned)blocks, threads, 0, st>>>(
+        (const Tt*)k, (const Tt*)v, (Tt*)k_cache, (Tt*)v_cache, slot_mapping, T, (int)H, (int)D,
+        (int)block_size, num_blocks * block_size, sk_t, sk_h, sv_t, sv_h, vec ? 1 : 0);
+    LSB_CHECK_LAUNCH("kv_cache_write");
+    return LSB_OK;
+  });
+}

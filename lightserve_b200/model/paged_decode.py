@@ -1,0 +1,209 @@
+"""Greedy decode over a paged KV cache, captured in a CUDA graph.
+
+This replaces lightserve's static-buffer full-recompute decode
+(``model/cuda_graph_decode.py:108-149``, which re-runs the whole causal
+forward over ``[B, max_seq_len]`` every step) with an incremental decode: one
+new token per sequence per step, its K/V written into a paged cache whose
+block tables come from ``lightserve_b200.engine.BlockManager`` (lightserve's
+``engine/block_manager.py`` API). The harness shape is the reference's:
+side-stream warm-up before capture (``:129-135``), one captured step
+(``:137-139``), replay per token, greedy ``argmax`` of the newest position's
+logits (``:114-118``).
+
+Per step and layer: fused add+RMSNorm (lsb kernel) -> fused QKV GEMM (cuBLAS)
+-> RoPE at each sequence's position -> ``write_kv_cache`` (lsb kernel) ->
+``paged_decode_attention`` (lsb kernel) -> O projection -> add+RMSNorm ->
+SwiGLU MLP. All buffers are static, so a step is graph-capturable.
+
+Block reservation: at admission the runner asks the block manager for every
+block the request will need over ``max_new_tokens`` (``allocate`` for the
+prompt, then the same ``append_slot`` sequence the scheduler would issue one
+token at a time), so replays never need new host-side table entries.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from ..engine import BlockManager, Request
+from ..kernels.fused_rmsnorm_residual import fused_add_rmsnorm
+from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
+                                        write_kv_cache)
+from .minimal_llama import LlamaConfig, LlamaWeights, apply_rope, llama_forward, precompute_rope
+
+
+class PagedKVCache:
+    """Per-layer K and V pools of shape [num_blocks, n_heads, block_size, head_dim]."""
+
+    def __init__(self, config: LlamaConfig, num_blocks: int, block_size: int = 16, device="cuda"):
+        shape = (num_blocks, config.n_heads, block_size, config.head_dim)
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.k = [torch.zeros(shape, dtype=config.dtype, device=device) for _ in range(config.n_layers)]
+        self.v = [torch.zeros(shape, dtype=config.dtype, device=device) for _ in range(config.n_layers)]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.k + self.v)
+
+
+def slots_for_positions(table, positions, block_size: int):
+    """Cache slots (block_id * block_size + offset) of token positions of one request."""
+    t = torch.as_tensor(table, dtype=torch.int64)
+    pos = torch.as_tensor(positions, dtype=torch.int64)
+    return t[pos // block_size] * block_size + pos % block_size
+
+
+@dataclass
+class _Fused:
+    w_qkv: torch.Tensor
+    w_gu: torch.Tensor
+
+
+class PagedDecoder:
+    """Runs prefill into the paged cache, then CUDA-graph greedy decode steps."""
+
+    def __init__(self, weights: LlamaWeights, config: LlamaConfig, cache: PagedKVCache,
+                 block_manager: BlockManager, max_batch: int, max_blocks_per_seq: int,
+                 device="cuda"):
+        self.w, self.cfg, self.cache, self.bm = weights, config, cache, block_manager
+        self.device = torch.device(device)
+        self.S, self.MB = max_batch, max_blocks_per_seq
+        self.fused = [_Fused(torch.cat([l.q_proj, l.k_proj, l.v_proj], dim=1).contiguous(),
+                             torch.cat([l.gate_proj, l.up_proj], dim=1).contiguous())
+                      for l in weights.layers]
+        self.cos, self.sin = precompute_rope(config, self.device)
+        S, Hd, H, D = max_batch, config.hidden_size, config.n_heads, config.head_dim
+        dev = self.device
+        self.tokens = torch.zeros(S, dtype=torch.int64, device=dev)
+        self.positions = torch.zeros(S, dtype=torch.int64, device=dev)
+        self.context_lens = torch.zeros(S, dtype=torch.int32, device=dev)
+        self.block_tables = torch.full((S, max_blocks_per_seq), -1, dtype=torch.int32, device=dev)
+        self.zeros = torch.zeros(S, Hd, dtype=config.dtype, device=dev)
+        self.attn_out = torch.empty(S, H, D, dtype=config.dtype, device=dev)
+        self.ws = paged_decode_workspace((S, H, D), max_blocks_per_seq, cache.block_size, dev)
+        self.graph = None
+        self.requests: list = []
+
+    # ------------------------------------------------------------ admission --
+    def admit(self, requests, max_new_tokens: int) -> torch.Tensor:
+        """Allocates blocks, runs each prompt's prefill into the cache and returns
+        the first greedy token of every request (int64 [len(requests)])."""
+        assert len(requests) <= self.S
+        bs = self.cache.block_size
+        first = []
+        for r in requests:
+            assert self.bm.can_allocate(r), f"not enough KV blocks for {r.request_id}"
+            self.bm.allocate(r)
+            # Reserve the decode blocks with the per-token append_slot sequence.
+            n0 = len(r.output_token_ids)
+            for _ in range(max_new_tokens + 1):
+                r.output_token_ids.append(-1)
+                self.bm.append_slot(r)
+            del r.output_token_ids[n0:]
+            table = self.bm.get_block_table(r)
+            assert len(table) <= self.MB, "max_blocks_per_seq too small"
+            ids = torch.tensor([r.prompt_token_ids], dtype=torch.int64, device=self.device)
+            n = ids.shape[1]
+            slots = slots_for_positions(table, range(n), bs).to(self.device)
+
+            def sink(li, k, v):
+                write_kv_cache(k[0].transpose(0, 1), v[0].transpose(0, 1), self.cache.k[li],
+                               self.cache.v[li], slots)
+
+            logits = llama_forward(self.w, self.cfg, ids, causal=True, kv_sink=sink, last_only=True)
+            first.append(logits[0, -1].argmax(-1))
+        self.requests = list(requests)
+        nreq = len(requests)
+        bt = self.bm.as_tensor(requests, self.MB)
+        self.block_tables.fill_(-1)
+        self.block_tables[:nreq].copy_(bt.to(self.device))
+        first_t = torch.stack(first).to(torch.int64)
+        self.tokens.zero_()
+        self.tokens[:nreq].copy_(first_t)
+        self.positions.zero_()
+        self.positions[:nreq].copy_(torch.tensor([len(r.prompt_token_ids) for r in requests],
+                                                 dtype=torch.int64, device=self.device))
+        return first_t
+
+    # ----------------------------------------------------------------- step --
+    def step(self) -> torch.Tensor:
+        """One greedy decode step over the static buffers; returns next tokens [S]."""
+        cfg, S, bs = self.cfg, self.S, self.cache.block_size
+        H, D, Hd, I = cfg.n_heads, cfg.head_dim, cfg.hidden_size, cfg.intermediate_size
+        pos = self.positions
+        self.context_lens.copy_(pos + 1)
+        blk = torch.gather(self.block_tables, 1, (pos // bs).unsqueeze(1)).squeeze(1).to(torch.int64)
+        slots = blk * bs + pos % bs
+        cos = self.cos[pos].unsqueeze(1)
+        sin = self.sin[pos].unsqueeze(1)
+        residual = F.embedding(self.tokens, self.w.embed_tokens)
+        x = self.zeros
+        for li, layer in enumerate(self.w.layers):
+            fz = self.fused[li]
+            normed, residual = fused_add_rmsnorm(x, residual, layer.input_layernorm_weight, eps=cfg.rms_eps)
+            qkv = (normed @ fz.w_qkv).view(S, 3, H, D)
+            q, k = apply_rope(qkv[:, 0], qkv[:, 1], cos, sin)
+            write_kv_cache(k, qkv[:, 2], self.cache.k[li], self.cache.v[li], slots)
+            attn = paged_decode_attention(q, self.cache.k[li], self.cache.v[li], self.block_tables,
+                                          self.context_lens, out=self.attn_out, workspace=self.ws)
+            x = attn.view(S, Hd) @ layer.o_proj
+            normed2, residual = fused_add_rmsnorm(x, residual, layer.post_attention_layernorm_weight,
+                                                  eps=cfg.rms_eps)
+            gu = normed2 @ fz.w_gu
+            x = (F.silu(gu[:, :I]) * gu[:, I:]) @ layer.down_proj
+        final, _ = fused_add_rmsnorm(x, residual, self.w.norm_weight, eps=cfg.rms_eps)
+        logits = final @ self.w.lm_head
+        nxt = logits.argmax(-1)
+        self.tokens.copy_(nxt)
+        self.positions.add_(1)
+        return self.tokens
+
+    def capture(self, warmup: int = 3):
+        """Side-stream warm-up, then capture one step into a CUDA graph.
+
+        Warm-up steps advance the positions and overwrite cache slots beyond
+        the prompt, so the state is saved and restored around them."""
+        saved = (self.tokens.clone(), self.positions.clone())
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.step()
+                self.tokens.copy_(saved[0]); self.positions.copy_(saved[1])
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        self.tokens.copy_(saved[0]); self.positions.copy_(saved[1])
+        self.graph = g
+        return g
+
+    def decode(self, num_steps: int, use_graph: bool = True) -> torch.Tensor:
+        """Runs num_steps steps; returns int64 [S, num_steps] generated tokens (on device)."""
+        hist = torch.empty(self.S, num_steps, dtype=torch.int64, device=self.device)
+        if use_graph and self.graph is None:
+            self.capture()
+        for i in range(num_steps):
+            if use_graph:
+                self.graph.replay()
+            else:
+                self.step()
+            hist[:, i].copy_(self.tokens)
+        return hist
+
+    def generate(self, requests, max_new_tokens: int, use_graph: bool = True):
+        """First token from prefill plus max_new_tokens - 1 decode steps, written back
+        to each request's output_token_ids; returns the token lists."""
+        first = self.admit(requests, max_new_tokens)
+        hist = self.decode(max_new_tokens - 1, use_graph=use_graph) if max_new_tokens > 1 else None
+        out = []
+        first = first.tolist()
+        h = hist.cpu().tolist() if hist is not None else None
+        for i, r in enumerate(requests):
+            toks = [first[i]] + (h[i] if h is not None else [])
+            r.output_token_ids.extend(toks)
+            out.append(toks)
+        return out
