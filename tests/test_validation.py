@@ -1,0 +1,63 @@
+"""The reference's argument checks (AssertionError before any launch), on CPU
+tensors: kernels/tests/test_flash_attention.py:80-122,
+kernels/tests/test_flash_attention_backward.py:127-139,
+kernels/tests/test_fused_rmsnorm_residual.py:80-96."""
+import pytest
+import torch
+
+from lightserve_b200.kernels import (flash_attention, flash_attention_forward, fused_add_rmsnorm,
+                                     paged_decode_attention)
+
+FNS = [flash_attention_forward, flash_attention]
+
+
+@pytest.mark.parametrize("fn", FNS)
+def test_rejects_shape_mismatch(fn):
+    with pytest.raises(AssertionError):
+        fn(torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 32), torch.randn(1, 2, 8, 32))
+
+
+@pytest.mark.parametrize("fn", FNS)
+def test_rejects_dtype_mismatch(fn):
+    with pytest.raises(AssertionError):
+        fn(torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 32, dtype=torch.float16), torch.randn(1, 2, 16, 32))
+
+
+@pytest.mark.parametrize("fn", FNS)
+def test_rejects_wrong_ndim(fn):
+    with pytest.raises(AssertionError):
+        fn(torch.randn(2, 16, 32), torch.randn(2, 16, 32), torch.randn(2, 16, 32))
+
+
+@pytest.mark.parametrize("fn", FNS)
+def test_rejects_cpu_tensor(fn):
+    with pytest.raises(AssertionError):
+        fn(torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 32))
+
+
+@pytest.mark.parametrize("fn", FNS)
+def test_rejects_head_dim_mismatch(fn):
+    with pytest.raises(AssertionError):
+        fn(torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 32), torch.randn(1, 2, 16, 64))
+
+
+def test_rmsnorm_rejects_shape_mismatch():
+    with pytest.raises(AssertionError):
+        fused_add_rmsnorm(torch.randn(4, 8), torch.randn(4, 9), torch.randn(8))
+
+
+def test_rmsnorm_rejects_noncontiguous_input():
+    with pytest.raises(AssertionError):
+        fused_add_rmsnorm(torch.randn(8, 4).t(), torch.randn(4, 8), torch.randn(8))
+
+
+def test_rmsnorm_rejects_cpu():
+    with pytest.raises(AssertionError):
+        fused_add_rmsnorm(torch.randn(4, 8), torch.randn(4, 8), torch.randn(8))
+
+
+def test_paged_decode_rejects_bad_tables():
+    q = torch.randn(2, 4, 64)
+    kc = torch.randn(8, 4, 16, 64)
+    with pytest.raises(AssertionError):
+        paged_decode_attention(q, kc, kc, torch.zeros(2, 4, dtype=torch.int64), torch.ones(2, dtype=torch.int32))
