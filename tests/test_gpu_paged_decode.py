@@ -54,8 +54,8 @@ def test_bad_block_ids_read_nothing():
     out = paged_decode_attention(q.cuda(), kc.cuda(), vc.cuda(), bt2.cuda(), cl.cuda())
     # tokens 32..39 live in block bt[1,2]; build the expected result from positions 0-15 and 32-39
     keep = [(int(bt[1, 0]), list(range(16))), (int(bt[1, 2]), list(range(8)))]
-    K = torch.cat([kc[b, :, offs] for b, offs in keep], dim=1).float()  # [H, 24, D]
-    V = torch.cat([vc[b, :, offs] for b, offs in keep], dim=1).float()
+    K = torch.cat([kc[b][:, offs] for b, offs in keep], dim=1).float()  # [H, 24, D]
+    V = torch.cat([vc[b][:, offs] for b, offs in keep], dim=1).float()
     s = torch.einsum("hd,hld->hl", q[1].float(), K) / 128 ** 0.5
     exp = torch.einsum("hl,hld->hd", s.softmax(-1), V)
     torch.testing.assert_close(out[1].float().cpu(), exp, atol=2e-2, rtol=2e-2)
