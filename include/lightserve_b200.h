@@ -46,6 +46,11 @@ extern "C" {
 /* Message describing the last failure on this thread ("" if none). */
 LSB_API const char* lsb_last_error(void);
 
+/* Nonzero if a kernel of this library gave up on a bounded on-chip wait (an
+ * mbarrier that never completed); the value names the wait. Reading it
+ * synchronises the device. 0 when no kernel ever timed out. */
+LSB_API int lsb_device_error(void);
+
 /* Library version string. */
 LSB_API const char* lsb_version(void);
 

@@ -16,4 +16,5 @@ int attn_bwd_tc(const void*, const void*, const void*, const void*, const void*,
   set_error("attn_bwd: tcgen05 kernel not built");
   return LSB_ERR_UNSUPPORTED;
 }
+int attn_bwd_tc_device_error() { return 0; }
 }  // namespace lsb

@@ -47,11 +47,20 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
                 const int64_t* sdv, float scale, int causal, int dtype, float* dsum,
                 float* dq_acc, cudaStream_t st);
 
+int attn_fwd_tc_device_error();
+int attn_bwd_tc_device_error();
+
 static inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 }  // namespace lsb
 
 extern "C" const char* lsb_last_error(void) { return lsb::g_err; }
+
+extern "C" int lsb_device_error(void) {
+  int e = lsb::attn_fwd_tc_device_error();
+  if (!e) e = lsb::attn_bwd_tc_device_error();
+  return e;
+}
 
 extern "C" const char* lsb_version(void) { return "lightserve_b200 0.1 (sm_100a)"; }
 
