@@ -67,6 +67,28 @@ struct Params {
 
 using namespace sm100;
 
+// Row max over a thread's 128 scores with 8 independent partial maxima; with
+// MASK, columns >= lim are set to -inf first (in place).
+template <bool MASK>
+__device__ __forceinline__ float row_max(uint32_t (&sr)[4][32], int lim) {
+  float mx8[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int cc = 0; cc < 32; ++cc) {
+      float v = __uint_as_float(sr[i][cc]);
+      if (MASK) {
+        v = (32 * i + cc < lim) ? v : -INFINITY;
+        sr[i][cc] = __float_as_uint(v);
+      }
+      mx8[cc & 7] = fmaxf(mx8[cc & 7], v);
+    }
+  return fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+}
+
 template <int D, int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -126,8 +148,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint8_t* sK = smem + L::K_OFF;
   uint8_t* sV = smem + L::V_OFF;
 
+  // Register split: 384 threads x 168 at launch = 128 x 56 (TMA/MMA warpgroup)
+  // + 256 x 224 (softmax warpgroups).
+  // (setmaxnreg sits at the top of each role's branch so ptxas budgets each.)
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
+    reg_dealloc<56>();
     if (lane == 0) {
       prefetch_tmap(&tq); prefetch_tmap(&tk); prefetch_tmap(&tv);
       mbar_arrive_expect_tx(q_full, TILES * KC * CHUNK_BYTES);
@@ -147,6 +173,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
+    reg_dealloc<56>();
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_f16(BM, BN, FMT, 0, 0);
       constexpr uint32_t IDESC_PV = idesc_f16(BM, D, FMT, 0, 1);
@@ -200,8 +227,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         mma_commit(&kv_empty[s]);
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    reg_dealloc<56>();  // warps 2-3: idle members of the TMA/MMA warpgroup
+  } else {
     // ------------------------------------------------------------- softmax --
+    reg_alloc<224>();
     const int t = (warp >> 2) - 1;
     const int row = threadIdx.x - 128 * (t + 1);          // TMEM lane of this thread
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
@@ -218,20 +248,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       for (int i = 0; i < 4; ++i) tmem_ld32(lane_addr + t * 128 + 32 * i, sr[i]);
       tmem_ld_wait();
       const int kv0 = j * BN;
+      // Only the diagonal tile (causal) and the tile holding position N-1 need masks.
       const bool need_mask = (kv0 + BN > p.N) || (p.causal && kv0 + BN - 1 > qt0);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          float v = __uint_as_float(sr[i][cc]);
-          if (need_mask) {
-            const int col = kv0 + 32 * i + cc;
-            if (col >= p.N || (p.causal && col > row_g)) v = -INFINITY;
-          }
-          sr[i][cc] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+      const int lim = min(p.N, p.causal ? row_g + 1 : p.N) - kv0;  // valid columns < lim
+      const float mx = need_mask ? row_max<true>(sr, lim) : row_max<false>(sr, lim);
       const float m_new = fmaxf(m, mx * sl2);
       float alpha = 1.f;
       const bool rescale = m_new > m + RESCALE_THRESHOLD;
@@ -241,6 +261,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         l *= alpha;
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
+      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t pk[16];
@@ -248,12 +269,14 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         for (int cc = 0; cc < 16; ++cc) {
           const float p0 = ex2(fmaf(__uint_as_float(sr[i][2 * cc]), sl2, -m_use));
           const float p1 = ex2(fmaf(__uint_as_float(sr[i][2 * cc + 1]), sl2, -m_use));
-          l += p0 + p1;
+          l8[(2 * cc) & 7] += p0;
+          l8[(2 * cc + 1) & 7] += p1;
           pk[cc] = FMT == 1 ? pack_bf16(p0, p1) : pack_f16(p0, p1);
         }
 #pragma unroll
         for (int cc = 0; cc < 16; ++cc) sr[i >> 1][(i & 1) * 16 + cc] = pk[cc];
       }
+      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
       tmem_st32(lane_addr + t * 128, sr[0]);
       tmem_st32(lane_addr + t * 128 + 32, sr[1]);
       if (rescale && j > 0) {

@@ -113,14 +113,16 @@ paged_decode_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
 #pragma unroll
     for (int off = 16; off >= LPT; off >>= 1)
       rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
-    const float m_new = fmaxf(m, rmax);  // finite: every round holds >= 1 valid token
-    const float alpha = exp2f(m - m_new);
+    // A round can be fully masked (bad block ids): keep the state unchanged then.
+    const float m_new = fmaxf(m, rmax);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float alpha = exp2f(m - m_use);
     l *= alpha;
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc[j] *= alpha;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float p = exp2f(sc[u] - m_new);  // 0 for masked rows
+      const float p = exp2f(sc[u] - m_use);  // 0 for masked rows
       l += p;
       if (ok[u]) {
 #pragma unroll

@@ -218,6 +218,16 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Warpgroup-wide register reallocation (all 4 warps of the warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ int elect_one_lane() { return (threadIdx.x & 31) == 0; }
 
 }  // namespace sm100
