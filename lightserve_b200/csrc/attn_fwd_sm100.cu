@@ -67,26 +67,35 @@ struct Params {
 
 using namespace sm100;
 
-// Row max over a thread's 128 scores with 8 independent partial maxima; with
-// MASK, columns >= lim are set to -inf first (in place).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Row max over a thread's 128 scores (three-input max, 8 independent partial
+// maxima for short dependency chains); with MASK, columns >= lim are set to
+// -inf first (in place).
 template <bool MASK>
 __device__ __forceinline__ float row_max(uint32_t (&sr)[4][32], int lim) {
+  if (MASK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int cc = 0; cc < 32; ++cc)
+        if (32 * i + cc >= lim) sr[i][cc] = __float_as_uint(-INFINITY);
+  }
   float mx8[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) mx8[u] = -INFINITY;
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int cc = 0; cc < 32; ++cc) {
-      float v = __uint_as_float(sr[i][cc]);
-      if (MASK) {
-        v = (32 * i + cc < lim) ? v : -INFINITY;
-        sr[i][cc] = __float_as_uint(v);
-      }
-      mx8[cc & 7] = fmaxf(mx8[cc & 7], v);
-    }
-  return fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+    for (int cc = 0; cc < 32; cc += 2)
+      mx8[(cc >> 1) & 7] = max3f(mx8[(cc >> 1) & 7], __uint_as_float(sr[i][cc]),
+                                 __uint_as_float(sr[i][cc + 1]));
+  return fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
+               max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
 }
 
 template <int D, int FMT>
@@ -261,22 +270,30 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         l *= alpha;
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
-      float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // Packed f32x2 arithmetic halves the instruction count of the scale and
+      // row-sum steps; the exponentials go to MUFU.EX2.
+      float2 l2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
+      const float2 sl2_2 = make_float2(sl2, sl2), negm2 = make_float2(-m_use, -m_use);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t pk[16];
 #pragma unroll
         for (int cc = 0; cc < 16; ++cc) {
-          const float p0 = ex2(fmaf(__uint_as_float(sr[i][2 * cc]), sl2, -m_use));
-          const float p1 = ex2(fmaf(__uint_as_float(sr[i][2 * cc + 1]), sl2, -m_use));
-          l8[(2 * cc) & 7] += p0;
-          l8[(2 * cc + 1) & 7] += p1;
-          pk[cc] = FMT == 1 ? pack_bf16(p0, p1) : pack_f16(p0, p1);
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i][2 * cc]),
+                                                  __uint_as_float(sr[i][2 * cc + 1])),
+                                      sl2_2, negm2);
+          const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+          l2[cc & 3] = __fadd2_rn(l2[cc & 3], pp);
+          pk[cc] = FMT == 1 ? pack_bf16(pp.x, pp.y) : pack_f16(pp.x, pp.y);
         }
 #pragma unroll
         for (int cc = 0; cc < 16; ++cc) sr[i >> 1][(i & 1) * 16 + cc] = pk[cc];
       }
-      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      {
+        const float2 a2 = __fadd2_rn(__fadd2_rn(l2[0], l2[1]), __fadd2_rn(l2[2], l2[3]));
+        l += a2.x + a2.y;
+      }
       tmem_st32(lane_addr + t * 128, sr[0]);
       tmem_st32(lane_addr + t * 128 + 32, sr[1]);
       if (rescale && j > 0) {
