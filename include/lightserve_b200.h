@@ -147,6 +147,25 @@ LSB_API int lsb_paged_decode(const void* q, const void* k_cache, const void* v_c
                      int64_t so_s, int64_t so_h, float scale, int dtype,
                      void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free paged decode. No counterpart exists in lightserve: this is
+ * lsb_paged_decode for callers that cannot allocate device memory (runtimes
+ * whose own pool owns the GPU's memory, FFI bindings without access to the
+ * host framework's allocator). The split-context scratch comes from a fixed
+ * 8 MiB array inside the library (lsb_paged_decode_static_scratch_capacity());
+ * sizes whose lsb_paged_decode_workspace_size exceeds it are rejected with
+ * LSB_ERR_INVALID. The first call on each device looks up the array's device
+ * address and should come before any stream capture. Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * Arguments are those of lsb_paged_decode without the workspace.
+ */
+LSB_API int64_t lsb_paged_decode_static_scratch_capacity(void);
+LSB_API int lsb_paged_decode_static_scratch(
+    const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables,
+    const int32_t* context_lens, void* o, int64_t S, int64_t H, int64_t D,
+    int64_t max_blocks_per_seq, int64_t block_size, int64_t num_blocks, int64_t sq_s,
+    int64_t sq_h, int64_t so_s, int64_t so_h, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

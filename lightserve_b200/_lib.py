@@ -54,6 +54,9 @@ SIGNATURES = {
     "lsb_paged_decode_workspace_size": (_I64, [_I64, _I64, _I64, _I64, _I64]),
     "lsb_paged_decode": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                               _I64, _I64, _I64, _I64, _F, _I, _P, _I64, _P]),
+    "lsb_paged_decode_static_scratch_capacity": (_I64, []),
+    "lsb_paged_decode_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                             _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
 }
 
 

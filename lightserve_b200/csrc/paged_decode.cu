@@ -22,6 +22,7 @@
 // caller-provided workspace and a combine kernel merges them.
 #include "common.cuh"
 
+#include <mutex>
 #include <type_traits>
 
 namespace lsb {
@@ -364,4 +365,80 @@ extern "C" int lsb_kv_cache_write(const void* k, const void* v, void* k_cache, v
     LSB_CHECK_LAUNCH("kv_cache_write");
     return LSB_OK;
   });
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of lsb_paged_decode.
+//
+// Some callers cannot allocate device memory for the split-context scratch:
+// runtimes that hand every byte of the GPU to their own memory pool (a
+// cudaMalloc from a plugin would bypass their budget or fail under it), and
+// thin FFI bindings (cgo, JNI, ctypes) that have no handle on the host
+// framework's allocator. For them this entry point keeps the scratch in a
+// fixed array inside the library instead of asking for a workspace.
+//
+// The array lives in every GPU that loads the library, until the process
+// exits. Its host-side name is not a device address, so the device address is
+// looked up once per device with cudaGetSymbolAddress (on that device's first
+// call, which should therefore come before any stream capture) and passed to
+// the kernels. Nothing in the array needs zeroing: every partial result the
+// combine step reads is written by the same call first. All calls share the
+// one array, so calls that overlap on the GPU (other streams, other threads)
+// race and must be serialised by the caller.
+namespace lsb {
+
+constexpr int64_t kPdStaticScratchBytes = 8ll << 20;  // 8 MiB
+static __device__ __align__(256) float g_pd_static_scratch[kPdStaticScratchBytes / 4];
+
+static void* pd_static_scratch_ptr(int* rc) {
+  static void* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("paged_decode_static_scratch: cannot determine the current device");
+    *rc = LSB_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_pd_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("paged_decode_static_scratch: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
+      *rc = LSB_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = LSB_OK;
+  return ptrs[dev];
+}
+
+}  // namespace lsb
+
+extern "C" int64_t lsb_paged_decode_static_scratch_capacity(void) {
+  return lsb::kPdStaticScratchBytes;
+}
+
+extern "C" int lsb_paged_decode_static_scratch(
+    const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables,
+    const int32_t* context_lens, void* o, int64_t S, int64_t H, int64_t D,
+    int64_t max_blocks_per_seq, int64_t block_size, int64_t num_blocks, int64_t sq_s,
+    int64_t sq_h, int64_t so_s, int64_t so_h, float scale, int dtype, void* stream) {
+  const int64_t need =
+      lsb_paged_decode_workspace_size(S, H, D, max_blocks_per_seq, block_size);
+  LSB_CHECK_ARG(need <= lsb::kPdStaticScratchBytes,
+                "paged_decode_static_scratch: these sizes need %lld bytes of scratch, above the "
+                "built-in %lld-byte maximum; use lsb_paged_decode with a caller workspace",
+                (long long)need, (long long)lsb::kPdStaticScratchBytes);
+  void* ws = nullptr;
+  if (need > 0) {
+    int rc = LSB_OK;
+    ws = lsb::pd_static_scratch_ptr(&rc);
+    if (rc) return rc;
+  }
+  return lsb_paged_decode(q, k_cache, v_cache, block_tables, context_lens, o, S, H, D,
+                          max_blocks_per_seq, block_size, num_blocks, sq_s, sq_h, so_s, so_h,
+                          scale, dtype, ws, need, stream);
 }
