@@ -241,7 +241,9 @@ def bench_decode(steps, warmup, ws, rank):
     reqs = [Request(f"r{i}", p) for i, p in enumerate(prompts)]
     dec.admit(reqs, c["steps"] + warmup + 1)
     dec.capture()
+    torch.cuda.nvtx.range_push("decode_steps")  # lets ncu select the timed replays
     total_ms, _ = time_cuda(dec.graph.replay, steps, warmup, ws)
+    torch.cuda.nvtx.range_pop()
     ms = total_ms / steps
     ctx = sum(lens) / len(lens) + warmup + steps / 2
     layers = cfg.n_layers

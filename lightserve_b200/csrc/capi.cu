@@ -49,6 +49,7 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
 
 int attn_fwd_tc_device_error();
 int attn_bwd_tc_device_error();
+int paged_decode_device_error();
 
 static inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
@@ -59,6 +60,7 @@ extern "C" const char* lsb_last_error(void) { return lsb::g_err; }
 extern "C" int lsb_device_error(void) {
   int e = lsb::attn_fwd_tc_device_error();
   if (!e) e = lsb::attn_bwd_tc_device_error();
+  if (!e) e = lsb::paged_decode_device_error();
   return e;
 }
 

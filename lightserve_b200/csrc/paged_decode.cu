@@ -21,6 +21,7 @@
 // the output directly; longer ones write (m, l, acc) partials to the
 // caller-provided workspace and a combine kernel merges them.
 #include "common.cuh"
+#include "sm100.cuh"
 
 #include <mutex>
 #include <type_traits>
@@ -207,6 +208,189 @@ paged_decode_combine_kernel(const int32_t* __restrict__ context_lens, int max_to
   }
 }
 
+// Bulk-copy variant (block_size 16): one producer warp streams whole
+// (block, head) runs of K and V -- BS*D contiguous elements each -- into a
+// PD_STAGES-deep shared-memory ring with cp.async.bulk + mbarrier
+// transaction counts, so every CTA keeps several KiB of HBM reads in flight
+// with few registers; four consumer warps each score a quarter of each
+// block's tokens from shared memory and keep the same online softmax as the
+// register kernel above. Partial results use the same workspace layout.
+constexpr int PD_STAGES = 4;
+constexpr int PD_BS = 16;
+
+template <typename T, int D>
+__global__ void __launch_bounds__((PD_WARPS + 1) * 32)
+paged_decode_bulk_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
+                         const T* __restrict__ v_cache, const int32_t* __restrict__ block_tables,
+                         const int32_t* __restrict__ context_lens, T* __restrict__ o, int H,
+                         int max_blocks, int num_blocks, int64_t sq_s, int64_t sq_h, int64_t so_s,
+                         int64_t so_h, float scale_log2, int max_parts, float* __restrict__ part_m,
+                         float* __restrict__ part_l, float* __restrict__ part_acc) {
+  using namespace sm100;
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int LPT = D / VEC;                    // lanes per token row
+  constexpr int TPW = 32 / LPT;                   // token rows per warp-wide load
+  constexpr int ROWS_PER_WARP = PD_BS / PD_WARPS; // rows of each block one warp scores
+  constexpr int U = (ROWS_PER_WARP + TPW - 1) / TPW;
+  constexpr int CH = PD_BS * D * (int)sizeof(T);  // bytes of one (block, head) run
+  constexpr int BLK_PER_PART = PD_PART_TOKENS / PD_BS;
+  static_assert(LPT >= 1 && LPT <= 32 && (32 % LPT) == 0, "unsupported head dim");
+  static_assert(CH % 16 == 0, "bulk copies move multiples of 16 bytes");
+
+  __shared__ __align__(128) uint8_t ring[PD_STAGES][2][CH];
+  __shared__ __align__(8) uint64_t full[PD_STAGES], empty[PD_STAGES];
+  __shared__ int valid[PD_STAGES];
+  __shared__ float sm_m[PD_WARPS], sm_l[PD_WARPS];
+  __shared__ float sm_acc[PD_WARPS][D];
+
+  const int part = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+  const int ctx = max(0, min(context_lens[s], max_blocks * PD_BS));
+  const int t_begin = part * PD_PART_TOKENS;
+  if (t_begin >= ctx && !(ctx == 0 && part == 0)) return;
+  const int t_end = min(ctx, t_begin + PD_PART_TOKENS);
+  const int nparts = (ctx + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
+  const int b0 = t_begin / PD_BS;
+  const int nblk = (t_end - t_begin + PD_BS - 1) / PD_BS;
+  (void)BLK_PER_PART;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PD_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], PD_WARPS);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int32_t* bt = block_tables + (int64_t)s * max_blocks;
+  const int64_t head_off = (int64_t)h * PD_BS * D;
+  const int64_t block_stride = (int64_t)H * PD_BS * D;
+
+  float m = -INFINITY, l = 0.f;
+  float acc[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+  const int grp = lane / LPT, dofs = (lane % LPT) * VEC;
+
+  if (warp == PD_WARPS) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      for (int i = 0; i < nblk; ++i) {
+        const int st = i % PD_STAGES;
+        if (i >= PD_STAGES && !mbar_wait(&empty[st], ((i / PD_STAGES) - 1) & 1, 0x401)) break;
+        const int blk = bt[b0 + i];
+        if (blk >= 0 && blk < num_blocks) {
+          valid[st] = 1;
+          mbar_arrive_expect_tx(&full[st], 2 * CH);
+          const int64_t off = blk * block_stride + head_off;
+          bulk_load(ring[st][0], k_cache + off, CH, &full[st]);
+          bulk_load(ring[st][1], v_cache + off, CH, &full[st]);
+        } else {
+          valid[st] = 0;  // a bad block id reads nothing; its tokens are masked
+          mbar_arrive(&full[st]);
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- consumers --
+    float qf[VEC];
+    {
+      Vec16<T> qv = ld_vec16(q + s * sq_s + h * sq_h + dofs);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) qf[j] = to_f(qv.v[j]) * scale_log2;
+    }
+    for (int i = 0; i < nblk; ++i) {
+      const int st = i % PD_STAGES;
+      if (!mbar_wait(&full[st], (i / PD_STAGES) & 1, 0x402)) break;
+      const int tok0 = t_begin + i * PD_BS;
+      const bool blk_ok = valid[st] != 0;
+      float sc[U];
+      Vec16<T> vv[U];
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int r = warp * ROWS_PER_WARP + u * TPW + grp;
+        const bool ok = blk_ok && (u * TPW + grp < ROWS_PER_WARP) && (tok0 + r < t_end);
+        float d = 0.f;
+        if (ok) {
+          Vec16<T> kv = *reinterpret_cast<const Vec16<T>*>(ring[st][0] + (r * D + dofs) * sizeof(T));
+          vv[u] = *reinterpret_cast<const Vec16<T>*>(ring[st][1] + (r * D + dofs) * sizeof(T));
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) d = fmaf(qf[j], to_f(kv.v[j]), d);
+        }
+#pragma unroll
+        for (int off = LPT / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+        sc[u] = ok ? d : -INFINITY;
+        rmax = fmaxf(rmax, sc[u]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+#pragma unroll
+      for (int off = 16; off >= LPT; off >>= 1)
+        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      const float m_new = fmaxf(m, rmax);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = exp2f(m - m_use);
+      l *= alpha;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] *= alpha;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float pw = exp2f(sc[u] - m_use);
+        l += pw;
+        if (sc[u] != -INFINITY) {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) acc[j] = fmaf(pw, to_f(vv[u].v[j]), acc[j]);
+        }
+      }
+      m = m_new;
+    }
+#pragma unroll
+    for (int off = 16; off >= LPT; off >>= 1) {
+      l += __shfl_xor_sync(0xffffffffu, l, off);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+    }
+    if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
+    if (grp == 0) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) sm_acc[warp][dofs + j] = acc[j];
+    }
+  }
+  __syncthreads();
+
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < PD_WARPS; ++w) M = fmaxf(M, sm_m[w]);
+  float wts[PD_WARPS];
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < PD_WARPS; ++w) {
+    wts[w] = (sm_m[w] == -INFINITY) ? 0.f : exp2f(sm_m[w] - M);
+    L += wts[w] * sm_l[w];
+  }
+  if (nparts <= 1) {
+    T* orow = o + s * so_s + h * so_h;
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < PD_WARPS; ++w) a = fmaf(wts[w], sm_acc[w][d], a);
+      orow[d] = from_f<T>(a * inv);
+    }
+  } else {
+    const int64_t pi = ((int64_t)s * H + h) * max_parts + part;
+    if (threadIdx.x == 0) { part_m[pi] = M; part_l[pi] = L; }
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < PD_WARPS; ++w) a = fmaf(wts[w], sm_acc[w][d], a);
+      part_acc[pi * D + d] = a;
+    }
+  }
+}
+
 template <typename T, int D>
 static int launch_paged_decode(const void* q, const void* kc, const void* vc,
                                const int32_t* bt, const int32_t* cl, void* o, int64_t S,
@@ -226,6 +410,16 @@ static int launch_paged_decode(const void* q, const void* kc, const void* vc,
     pa = pl + S * H * P;
   }
   dim3 grid((unsigned)P, (unsigned)H, (unsigned)S);
+  bool launched = false;
+  if constexpr (PD_BS * D * sizeof(T) * 2 * PD_STAGES <= 40 * 1024) {
+    if (bs_log2 == 4 && aligned16(kc) && aligned16(vc)) {
+      paged_decode_bulk_kernel<T, D><<<grid, (PD_WARPS + 1) * 32, 0, st>>>(
+          (const T*)q, (const T*)kc, (const T*)vc, bt, cl, (T*)o, (int)H, (int)max_blocks,
+          (int)num_blocks, sq_s, sq_h, so_s, so_h, scale * PD_LOG2E, (int)P, pm, pl, pa);
+      launched = true;
+    }
+  }
+  if (!launched)
   paged_decode_kernel<T, D><<<grid, PD_WARPS * 32, 0, st>>>(
       (const T*)q, (const T*)kc, (const T*)vc, bt, cl, (T*)o, (int)H, (int)max_blocks, (int)num_blocks, bs_log2,
       sq_s, sq_h, so_s, so_h, scale * PD_LOG2E, (int)P, pm, pl, pa);
@@ -268,6 +462,12 @@ __global__ void kv_cache_write_kernel(const T* __restrict__ k, const T* __restri
       v_cache[dst + d] = vs[d];
     }
   }
+}
+
+int paged_decode_device_error() {
+  int e = 0;
+  cudaMemcpyFromSymbol(&e, sm100::g_lsb_device_error, sizeof(int));
+  return e;
 }
 
 }  // namespace lsb
