@@ -250,7 +250,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv_t[t]; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, 0x301)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_full[t], j & 1, 0x301)) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
@@ -296,7 +296,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       }
       tmem_st32(lane_addr + t * 128, sr[0]);
       tmem_st32(lane_addr + t * 128 + 32, sr[1]);
-      if (rescale && j > 0) {
+      // tcgen05.ld/st are warp-collective: if any row of the warp rescales,
+      // the whole warp runs the loop (alpha is 1 for rows that do not).
+      if (__any_sync(0xffffffffu, rescale && j > 0)) {
+        if (!(rescale && j > 0)) alpha = 1.f;
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) {
           uint32_t ov[32];
@@ -311,7 +314,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       tc_fence_before();
       mbar_arrive(&p_full[t]);
     }
-    if (ok && nkv_t[t] > 0 && mbar_wait(&pv_done[t], (nkv_t[t] - 1) & 1, 0x302)) {
+    if (ok && nkv_t[t] > 0 && mbar_wait_warp(&pv_done[t], (nkv_t[t] - 1) & 1, 0x302)) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +

@@ -75,6 +75,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
   return true;
 }
 
+// Warp-uniform wait for roles whose next instructions are warp-collective
+// (tcgen05.ld/st): either every lane proceeds or every lane gives up.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, code)) != 0;
+}
+
 // ------------------------------------------------------------------ TMA ---
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2, int c3) {
