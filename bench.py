@@ -58,13 +58,9 @@ def barrier(ws):
 
 
 def max_over_ranks(x: float, ws: int) -> float:
-    if ws == 1:
-        return x
-    import torch.distributed as dist
+    from lightserve_b200.sharding import max_over_ranks as _m
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return _m(x) if ws > 1 else x
 
 
 def load_peaks():
@@ -155,14 +151,21 @@ def _randn(shape, dtype, gen):
     return torch.randn(*shape, device="cuda", dtype=torch.float32, generator=gen).to(dtype)
 
 
-def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps):
+def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
     from lightserve_b200.kernels import flash_attention_forward
+    from lightserve_b200.sharding import shard_range
     from oracle.attention import attn_fwd_flops
 
     c = FWD_CFG
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(3))
-    flops = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], c["causal"])
+    if strong:  # this rank's contiguous share of the B*H (b, h) slices
+        a, b = shard_range(c["B"] * c["H"], rank, ws)
+        shape = (1, b - a, c["N"], c["D"])
+    else:       # every rank runs the full config on its own slices
+        shape = (c["B"], c["H"], c["N"], c["D"])
+    q, k, v = (_randn(shape, torch.bfloat16, gen) for _ in range(3))
+    flops = attn_fwd_flops(shape[0], shape[1], c["N"], c["D"], c["causal"])
+    mult = 1 if strong else ws  # whole-job work = per-rank work x ranks (weak)
     total_ms, per = time_cuda(lambda: flash_attention_forward(q, k, v, causal=True), steps, warmup, ws)
     ms = total_ms / steps
     kern_ms = statistics.mean(per)
@@ -181,9 +184,11 @@ def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps):
     nb = q.numel() * q.element_size()
     return {
         "ms": ms, "kernel_ms": kern_ms, "flops": flops,
-        "value": ws * flops / (ms * 1e-3) / 1e12,
+        "value": (attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) if strong else mult * flops)
+        / (ms * 1e-3) / 1e12,
         "kernel_tflops": flops / (kern_ms * 1e-3) / 1e12,
-        "e2e": {"value": ws * flops / (e2e_total / e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "e2e": {"value": (attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) if strong else mult * flops)
+                / (e2e_total / e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 3 * nb, "d2h_bytes_per_step": nb, "steps": e2e_steps},
         "launches_per_step": 1,
     }
@@ -326,6 +331,8 @@ def main():
     ap.add_argument("--only", default="fwd,bwd,rmsnorm,decode",
                     help="comma list of workloads (fwd is always run: it is the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--strong", action="store_true",
+                    help="split config 2's (b,h) slices across ranks instead of one full config per rank")
     args = ap.parse_args()
     rank, ws, local = dist_setup()
     if args.impl == "reference":
@@ -336,7 +343,8 @@ def main():
     traffic = load_traffic()
     only = set(args.only.split(","))
     with ClockSampler(local) as clk:
-        fwd = bench_fwd(args.steps, args.warmup, ws, rank, peaks, e2e_steps=min(args.steps, 5))
+        fwd = bench_fwd(args.steps, args.warmup, ws, rank, peaks, e2e_steps=min(args.steps, 5),
+                        strong=args.strong)
     secondary = {}
     if "bwd" in only:
         secondary["fa_bwd"] = bench_bwd(args.steps, args.warmup, ws, rank)
@@ -356,7 +364,8 @@ def main():
     tr = traffic.get("attn_fwd", {}).get("dram_bytes_per_launch")
     line = {
         "metric": METRIC, "value": fwd["value"], "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": fwd["ms"], "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": fwd["ms"], "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))", "config": CONFIG,
         "e2e": {k: v for k, v in fwd["e2e"].items() if k != "steps"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
