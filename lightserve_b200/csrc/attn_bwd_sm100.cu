@@ -13,15 +13,17 @@
 // transposed so the 128 keys are the TMEM lanes:
 //   S^T  = K Q^T      (SS MMA)  -> TMEM cols [0,64)
 //   dP^T = V dO^T     (SS MMA)  -> TMEM cols [64,128)
-//   dV  += P^T dO     (TS MMA, P^T written as 16-bit over S^T) -> [128,256)
-//   dK  += dS^T Q     (TS MMA, dS^T written over dP^T)         -> [256,384)
+//   dV  += P^T dO     (TS MMA, P^T packed to 16 bits over S^T)  -> [128,256)
+//   dK  += dS^T Q     (TS MMA, dS^T packed over dP^T)           -> [256,384)
 //   dQ^T = K^T dS^T   (SS MMA, K^T read MN-major from the K tile, dS^T
-//                      from a 128-byte-swizzled shared tile)   -> [384,448)
-// Warp 0 streams K/V once and Q/dO tiles through a 2-stage ring (TMA);
-// warp 1 owns TMEM and issues the MMAs; warpgroup 1 (one thread per key)
-// turns S^T/dP^T into P^T/dS^T; warpgroup 2 (one thread per head-dim index)
-// reads each dQ^T tile and adds it into the fp32 dQ buffer with coalesced
-// reductions (32 consecutive head-dim columns per warp instruction).
+//                      from a 128-byte-swizzled shared tile)    -> [384,448)
+// Warp 0 streams K/V once and Q/dO tiles (plus each tile's log-sum-exp and
+// Dsum) through a 2-stage ring; warp 1 owns TMEM and issues the MMAs; warp 2
+// adds each finished 64-row dQ tile into the fp32 dQ buffer with one bulk
+// shared->global reduction (double-buffered staging). Warpgroups 1 and 2 split
+// every tile's 64 query columns: thread = key for P^T / dS^T, thread =
+// head-dim index when staging dQ^T; the previous tile's dQ^T is staged while
+// the current dP^T completes.
 // All mbarrier waits are bounded (sm100.cuh).
 #include "common.cuh"
 #include "sm100.cuh"
@@ -56,9 +58,10 @@ constexpr int V_OFF = K_OFF + KC * KV_CHUNK;
 constexpr int Q_OFF = V_OFF + KC * KV_CHUNK;          // [2 stages][KC] Q chunks
 constexpr int DO_OFF = Q_OFF + 2 * KC * Q_CHUNK;      // [2 stages][KC] dO chunks
 constexpr int DS_OFF = DO_OFF + 2 * KC * Q_CHUNK;     // dS^T [128 keys][64 q] swizzled
-constexpr int STAT_OFF = DS_OFF + BN * BM * 2;        // [2][2][64] floats: lse2, dsum
+constexpr int RED_OFF = DS_OFF + BN * BM * 2;         // dQ staging [2 bufs][64 q][D] fp32
+constexpr int STAT_OFF = RED_OFF + 2 * BM * D * 4;    // [2][2][64] floats: lse2, dsum
 constexpr int BAR_OFF = STAT_OFF + 2 * 2 * BM * 4;
-constexpr int NBAR = 1 + 2 + 2 + 8;
+constexpr int NBAR = 1 + 2 + 2 + 8 + 2 + 4;
 constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
 constexpr int SMEM = SLOT_OFF + 16 + 1024;
 
@@ -84,6 +87,20 @@ __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+#ifdef LSB_BWD_TRACE
+// Debug-build timeline of CTA (0, 0): clock64 per event and query tile.
+__device__ long long g_bwd_trace[16][64];
+#define BWD_TRACE(cond, ev, it)                                               \
+  do {                                                                        \
+    if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && (it) < 64)            \
+      g_bwd_trace[ev][it] = clock64();                                        \
+  } while (0)
+#else
+#define BWD_TRACE(cond, ev, it) \
+  do {                          \
+  } while (0)
+#endif
+
 template <int FMT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return FMT == 1 ? pack_bf16(a, b) : pack_f16(a, b);
@@ -108,6 +125,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint64_t* dk_done = bars + 10;
   uint64_t* dq_ready = bars + 11;
   uint64_t* dq_free = bars + 12;
+  uint64_t* stat_full = bars + 13;  // [2]: per-stage log-sum-exp / Dsum staged
+  float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [2][lse2 64 | dsum 64]
+  uint64_t* red_full = bars + 15;  // [2 bufs]: dQ tile staged (256 arrivals)
+  uint64_t* red_free = bars + 17;  // [2 bufs]: its bulk reduction has read it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SLOT_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -124,12 +145,15 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     for (int s = 0; s < 2; ++s) { mbar_init(&q_full[s], 1); mbar_init(&q_empty[s], 1); }
     mbar_init(s_ready, 1);
     mbar_init(dp_ready, 1);
-    mbar_init(p_ready, 128);
-    mbar_init(ds_ready, 128);
+    mbar_init(p_ready, 256);
+    mbar_init(ds_ready, 256);
     mbar_init(dv_done, 1);
     mbar_init(dk_done, 1);
     mbar_init(dq_ready, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 256);
+    mbar_init(&stat_full[0], 32);
+    mbar_init(&stat_full[1], 32);
+    for (int i = 0; i < 2; ++i) { mbar_init(&red_full[i], 256); mbar_init(&red_free[i], 1); }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -149,7 +173,9 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
-    reg_dealloc<64>();
+    reg_dealloc<72>();
+    const float* lse_bh = p.lse + (int64_t)bh * p.N;
+    const float* dsum_bh = p.dsum + (int64_t)bh * p.N;
     if (lane == 0) {
       prefetch_tmap(&tq); prefetch_tmap(&tk); prefetch_tmap(&tv); prefetch_tmap(&tdo);
       mbar_arrive_expect_tx(kv_full, 2 * KC * KV_CHUNK);
@@ -157,20 +183,34 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tma_load_4d(sK + kc * KV_CHUNK, &tk, kv_full, kc * 64, kv0, h, b);
         tma_load_4d(sV + kc * KV_CHUNK, &tv, kv_full, kc * 64, kv0, h, b);
       }
-      for (int it = 0; it < n; ++it) {
-        const int s = it & 1;
-        if (it >= 2 && !mbar_wait(&q_empty[s], ((it >> 1) - 1) & 1, 0x501)) break;
-        const int m0 = (i0 + it) * BM;
+    }
+    for (int it = 0; it < n; ++it) {
+      const int s = it & 1;
+      // Stage s is reused once the MMAs of tile it-2 (and so every read of
+      // its statistics, which precede ds_ready) have completed.
+      if (it >= 2 && !mbar_wait_warp(&q_empty[s], ((it >> 1) - 1) & 1, 0x501)) break;
+      const int m0 = (i0 + it) * BM;
+      if (lane == 0) {
         mbar_arrive_expect_tx(&q_full[s], 2 * KC * Q_CHUNK);
         for (int kc = 0; kc < KC; ++kc) {
           tma_load_4d(sQ + (s * KC + kc) * Q_CHUNK, &tq, &q_full[s], kc * 64, m0, h, b);
           tma_load_4d(sDO + (s * KC + kc) * Q_CHUNK, &tdo, &q_full[s], kc * 64, m0, h, b);
         }
       }
+      // Per-query statistics of this tile: log2-scaled LSE and Dsum.
+      float* st = stats + s * 2 * BM;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int c = lane + 32 * u;
+        const bool in = m0 + c < p.N;
+        st[c] = in ? __ldg(lse_bh + m0 + c) * 1.4426950408889634f : 0.f;
+        st[BM + c] = in ? __ldg(dsum_bh + m0 + c) : 0.f;
+      }
+      mbar_arrive(&stat_full[s]);
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
-    reg_dealloc<64>();
+    reg_dealloc<72>();
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, BM, FMT, 0, 0);   // K-major A and B
       constexpr uint32_t ID_DV = idesc_f16(128, D, FMT, 0, 1);   // B (dO, Q) MN-major
@@ -191,7 +231,12 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk) {
           const uint64_t bd = smem_desc_sw128(b_base + kk * 2048, Q_CHUNK, 1024);
-          mma_ts(tmem + d_col, tmem + a_col + kk * 8, bd, ID_DV, (acc || kk > 0) ? 1u : 0u);
+          // Each warpgroup packs its 32 query columns into the first 16 TMEM
+          // columns of its own 32-column fp32 half, so the other warpgroup's
+          // unread scores are never overwritten: K-steps 0-1 read [0,16),
+          // K-steps 2-3 read [32,48) of the buffer.
+          mma_ts(tmem + d_col, tmem + a_col + (kk >> 1) * 32 + (kk & 1) * 8, bd, ID_DV,
+                 (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(kv_full, 0, 0x601) && mbar_wait(&q_full[0], 0, 0x602);
@@ -199,6 +244,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tc_fence_after();
         issue_t(T_S, k_base, q_base);
         mma_commit(s_ready);
+        BWD_TRACE(true, 1, 0);
         issue_t(T_DP, v_base, do_base);
         mma_commit(dp_ready);
       }
@@ -206,9 +252,11 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         const int s = it & 1;
         const uint32_t ph = it & 1;
         if (!mbar_wait(p_ready, ph, 0x603)) { ok = false; break; }
+        BWD_TRACE(true, 2, it);
         tc_fence_after();
         issue_acc(T_DV, T_S, do_base + s * KC * Q_CHUNK, it > 0);
         mma_commit(dv_done);
+        BWD_TRACE(true, 3, it);
         if (it + 1 < n) {
           const int s1 = (it + 1) & 1;
           // S^T(it+1) overwrites P^T(it): wait until dV(it) has read it.
@@ -217,11 +265,14 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           tc_fence_after();
           issue_t(T_S, k_base, q_base + s1 * KC * Q_CHUNK);
           mma_commit(s_ready);
+          BWD_TRACE(true, 1, it + 1);
         }
         if (!mbar_wait(ds_ready, ph, 0x606)) { ok = false; break; }
+        BWD_TRACE(true, 4, it);
         tc_fence_after();
         issue_acc(T_DK, T_DP, q_base + s * KC * Q_CHUNK, it > 0);
         mma_commit(dk_done);
+        BWD_TRACE(true, 5, it);
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x607)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -231,6 +282,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           mma_ss(tmem + T_DQ, a, bd, ID_DQ, kk > 0);
         }
         mma_commit(dq_ready);
+        BWD_TRACE(true, 6, it);
         mma_commit(&q_empty[s]);
         if (it + 1 < n) {
           const int s1 = (it + 1) & 1;
@@ -242,140 +294,164 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
       }
     }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------- dQ reducer --
+    // Adds each staged 64-row dQ tile into the fp32 dQ buffer (rows are
+    // contiguous there) with one bulk reduction; two staging buffers let the
+    // next tile be staged while this one is being read.
+    reg_dealloc<72>();
+    if (lane == 0) {
+      for (int it = 0; it < n; ++it) {
+        const int bsel = it & 1;
+        if (!mbar_wait(&red_full[bsel], (it >> 1) & 1, 0x901)) break;
+        const int m0 = (i0 + it) * BM;
+        const int rows = min(BM, p.N - m0);
+        bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + m0) * D,
+                            reinterpret_cast<const float*>(smem + RED_OFF) + bsel * BM * D,
+                            rows * D * 4);
+        bulk_commit();
+        bulk_wait_read_1();  // the previous tile's reduction has read its buffer
+        if (it > 0) mbar_arrive(&red_free[bsel ^ 1]);
+      }
+      bulk_wait_all();  // every reduction has landed before the CTA exits
+    }
   } else if (warp < 4) {
-    reg_dealloc<64>();
-  } else if (warp < 8) {
-    // ------------------------------------------- P^T / dS^T (thread = key) --
-    reg_alloc<240>();
-    const int r = threadIdx.x - 128;
+    reg_dealloc<72>();
+  } else {
+    // ------------------------------------------------------------------------
+    // Two warpgroups split the 64 query columns of each tile (32 each):
+    // thread = key (TMEM lane) for P^T / dS^T, then thread = head-dim index
+    // for its half of the dQ^T columns. Epilogue: warpgroup 1 writes dV,
+    // warpgroup 2 writes dK.
+    reg_alloc<216>();
+    const int half = warp >> 3;                  // 0: q cols [0,32), 1: [32,64)
+    const int r = (threadIdx.x & 127);           // TMEM lane: key, then head-dim index
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const int key = kv0 + r;
     const float sl2 = p.scale_log2;
-    const float* lse_bh = p.lse + (int64_t)bh * p.N;
-    const float* dsum_bh = p.dsum + (int64_t)bh * p.N;
+    const int cb = half * 32;                    // first query column of this half
+    // dQ^T columns [cb, cb+32) of tile jt: thread = head-dim index r. The 32
+    // query rows are staged [q][d] in shared memory; warp 2 adds the whole
+    // 64-row tile into the fp32 dQ buffer with one bulk reduction.
+    auto stage_dq = [&](int jt) -> bool {
+      if (!mbar_wait_warp(dq_ready, jt & 1, 0x801)) return false;
+      BWD_TRACE(r == 0 && half == 0, 11, jt);
+      tc_fence_after();
+      uint32_t qv[32];
+      tmem_ld32(lane_addr + T_DQ + cb, qv);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(dq_free);
+      const int bsel = jt & 1;
+      if (jt >= 2 && !mbar_wait_warp(&red_free[bsel], ((jt >> 1) - 1) & 1, 0x802)) return false;
+      float* stage = reinterpret_cast<float*>(smem + RED_OFF) + bsel * BM * D + half * 32 * D;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) stage[c * D + r] = __uint_as_float(qv[c]) * p.scale;
+      fence_proxy_async_smem();
+      mbar_arrive(&red_full[bsel]);
+      BWD_TRACE(r == 0 && half == 0, 12, jt);
+      return true;
+    };
     bool ok = true;
     for (int it = 0; it < n; ++it) {
       const uint32_t ph = it & 1;
       const int m0 = (i0 + it) * BM;
+      const float* st = stats + (it & 1) * 2 * BM;
+      if (!mbar_wait_warp(&stat_full[it & 1], (it >> 1) & 1, 0x705)) { ok = false; break; }
       if (!mbar_wait_warp(s_ready, ph, 0x701)) { ok = false; break; }
+      BWD_TRACE(r == 0 && half == 0, 7, it);
       tc_fence_after();
-      uint32_t sv[2][32];
-      tmem_ld32(lane_addr + T_S, sv[0]);
-      tmem_ld32(lane_addr + T_S + 32, sv[1]);
+      uint32_t sv[32];
+      tmem_ld32(lane_addr + T_S + cb, sv);
       tmem_ld_wait();
       // Masks: causal (q < key), and rows/columns past the sequence end.
       const bool need_mask = (m0 + BM > p.N) || (kv0 + BN > p.N) || (p.causal && m0 < kv0 + BN);
       const int qlo = p.causal ? key : 0;  // first valid q for this key
-      float pf[64];
+      float pf[32];
+      uint32_t pk[16];
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          const int c0 = h2 * 32 + 2 * cc;
-          // Per-column log-sum-exp (broadcast reads, L1-resident after the first warp).
-          const float la = __ldg(lse_bh + min(m0 + c0, p.N - 1)) * 1.4426950408889634f;
-          const float lb = __ldg(lse_bh + min(m0 + c0 + 1, p.N - 1)) * 1.4426950408889634f;
-          float p0 = ex2(fmaf(__uint_as_float(sv[h2][2 * cc]), sl2, -la));
-          float p1 = ex2(fmaf(__uint_as_float(sv[h2][2 * cc + 1]), sl2, -lb));
-          if (need_mask) {
-            const int q0 = m0 + c0;
-            if (key >= p.N || q0 >= p.N || q0 < qlo) p0 = 0.f;
-            if (key >= p.N || q0 + 1 >= p.N || q0 + 1 < qlo) p1 = 0.f;
-          }
-          pf[c0] = p0;
-          pf[c0 + 1] = p1;
-          pk[cc] = pack2<FMT>(p0, p1);
+      for (int cc = 0; cc < 16; ++cc) {
+        const int c0 = cb + 2 * cc;
+        const float2 l2 = *reinterpret_cast<const float2*>(st + c0);  // shared broadcast
+        float p0 = ex2(fmaf(__uint_as_float(sv[2 * cc]), sl2, -l2.x));
+        float p1 = ex2(fmaf(__uint_as_float(sv[2 * cc + 1]), sl2, -l2.y));
+        if (need_mask) {
+          const int q0 = m0 + c0;
+          if (key >= p.N || q0 >= p.N || q0 < qlo) p0 = 0.f;
+          if (key >= p.N || q0 + 1 >= p.N || q0 + 1 < qlo) p1 = 0.f;
         }
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) sv[0][h2 * 16 + cc] = pk[cc];
+        pf[2 * cc] = p0;
+        pf[2 * cc + 1] = p1;
+        pk[cc] = pack2<FMT>(p0, p1);
       }
-      tmem_st32(lane_addr + T_S, sv[0]);
+      tmem_st16(lane_addr + T_S + half * 32, pk);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_ready);
+      BWD_TRACE(r == 0 && half == 0, 8, it);
+      // The previous tile's dQ^T (ready by now) is staged while dP^T(it) finishes.
+      if (it > 0 && !stage_dq(it - 1)) { ok = false; break; }
 
       if (!mbar_wait_warp(dp_ready, ph, 0x702)) { ok = false; break; }
+      BWD_TRACE(r == 0 && half == 0, 9, it);
       tc_fence_after();
-      tmem_ld32(lane_addr + T_DP, sv[0]);
-      tmem_ld32(lane_addr + T_DP + 32, sv[1]);
+      tmem_ld32(lane_addr + T_DP + cb, sv);
       tmem_ld_wait();
-      uint32_t dsk[32];
+      uint32_t dsk[16];
 #pragma unroll
-      for (int cc = 0; cc < 32; ++cc) {
-        const int c0 = 2 * cc;
-        const float2 ds2 = make_float2(__ldg(dsum_bh + min(m0 + c0, p.N - 1)),
-                                       __ldg(dsum_bh + min(m0 + c0 + 1, p.N - 1)));
-        const float a = pf[c0] * (__uint_as_float(sv[c0 >> 5][c0 & 31]) - ds2.x);
-        const float bq = pf[c0 + 1] * (__uint_as_float(sv[(c0 + 1) >> 5][(c0 + 1) & 31]) - ds2.y);
-        dsk[cc] = pack2<FMT>(a, bq);
+      for (int cc = 0; cc < 16; ++cc) {
+        const float2 ds2 = *reinterpret_cast<const float2*>(st + BM + cb + 2 * cc);
+        dsk[cc] = pack2<FMT>(pf[2 * cc] * (__uint_as_float(sv[2 * cc]) - ds2.x),
+                             pf[2 * cc + 1] * (__uint_as_float(sv[2 * cc + 1]) - ds2.y));
       }
-      tmem_st32(lane_addr + T_DP, dsk);
-      // dS^T row -> shared (128-byte swizzle) for the dQ^T GEMM, once the
+      tmem_st16(lane_addr + T_DP + half * 32, dsk);
+      // dS^T row half -> shared (128-byte swizzle) for the dQ^T GEMM, once the
       // previous dQ^T GEMM has finished reading the buffer.
-      if (it > 0 && !mbar_wait_warp(dq_ready, (it - 1) & 1, 0x703)) { ok = false; break; }
+      // (dQ^T(it-1) has completed -- stage_dq waited for it -- so the dQ GEMM
+      // no longer reads the dS^T buffer.)
       {
         uint8_t* rowp = sDS + r * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) =
+        for (int c = 0; c < 4; ++c) {
+          const int chunk = half * 4 + c;
+          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(dsk[4 * c], dsk[4 * c + 1], dsk[4 * c + 2], dsk[4 * c + 3]);
+        }
       }
       fence_proxy_async_smem();
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(ds_ready);
+      BWD_TRACE(r == 0 && half == 0, 10, it);
+
     }
-    // Epilogue: dV and dK rows of this thread's key.
+    if (ok && !stage_dq(n - 1)) ok = false;
+    // Epilogue: warpgroup 1 writes this key's dV row, warpgroup 2 its dK row.
     if (ok && mbar_wait_warp(dk_done, (n - 1) & 1, 0x704)) {
       tc_fence_after();
       // tcgen05.ld is warp-collective: every lane loads, only valid keys store.
       const bool store = key < p.N;
-      uint8_t* dvr = reinterpret_cast<uint8_t*>(p.dv) + 2 * (b * p.sdv_b + h * p.sdv_h + (int64_t)key * p.sdv_n);
-      uint8_t* dkr = reinterpret_cast<uint8_t*>(p.dk) + 2 * (b * p.sdk_b + h * p.sdk_h + (int64_t)key * p.sdk_n);
+      const uint32_t col = half == 0 ? T_DV : T_DK;
+      const float mul = half == 0 ? 1.f : p.scale;
+      uint8_t* dst = half == 0
+          ? reinterpret_cast<uint8_t*>(p.dv) + 2 * (b * p.sdv_b + h * p.sdv_h + (int64_t)key * p.sdv_n)
+          : reinterpret_cast<uint8_t*>(p.dk) + 2 * (b * p.sdk_b + h * p.sdk_h + (int64_t)key * p.sdk_n);
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t col = which == 0 ? T_DV : T_DK;
-        const float mul = which == 0 ? 1.f : p.scale;
-        uint8_t* dst = which == 0 ? dvr : dkr;
+      for (int i = 0; i < D / 32; ++i) {
+        uint32_t v[32];
+        tmem_ld32(lane_addr + col + 32 * i, v);
+        tmem_ld_wait();
+        uint32_t pk2[16];
 #pragma unroll
-        for (int i = 0; i < D / 32; ++i) {
-          uint32_t v[32];
-          tmem_ld32(lane_addr + col + 32 * i, v);
-          tmem_ld_wait();
-          uint32_t pk[16];
+        for (int cc = 0; cc < 16; ++cc)
+          pk2[cc] = pack2<FMT>(__uint_as_float(v[2 * cc]) * mul, __uint_as_float(v[2 * cc + 1]) * mul);
+        if (store) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 64 * i);
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc)
-            pk[cc] = pack2<FMT>(__uint_as_float(v[2 * cc]) * mul, __uint_as_float(v[2 * cc + 1]) * mul);
-          if (store) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + 64 * i);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4)
-              d4[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
-          }
+          for (int v4 = 0; v4 < 4; ++v4)
+            d4[v4] = make_uint4(pk2[4 * v4], pk2[4 * v4 + 1], pk2[4 * v4 + 2], pk2[4 * v4 + 3]);
         }
       }
-    }
-  } else {
-    // ----------------------------------------------- dQ reduction (thread = d) --
-    reg_alloc<200>();
-    const int d = threadIdx.x - 256;
-    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    float* dq_bh = p.dq_acc + (int64_t)bh * p.N * D + d;
-    for (int it = 0; it < n; ++it) {
-      if (!mbar_wait_warp(dq_ready, it & 1, 0x801)) break;
-      tc_fence_after();
-      uint32_t v[2][32];
-      tmem_ld32(lane_addr + T_DQ, v[0]);
-      tmem_ld32(lane_addr + T_DQ + 32, v[1]);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      const int m0 = (i0 + it) * BM;
-      const int lim = min(BM, p.N - m0);
-#pragma unroll
-      for (int c = 0; c < BM; ++c)
-        if (c < lim) atomicAdd(dq_bh + (int64_t)(m0 + c) * D, __uint_as_float(v[c >> 5][c & 31]) * p.scale);
     }
   }
 
@@ -463,6 +539,12 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   return bf ? launch_dq_cast<__nv_bfloat16>(dq_acc, dq, B, H, N, D, S4(sdq), st)
             : launch_dq_cast<__half>(dq_acc, dq, B, H, N, D, S4(sdq), st);
 }
+
+#ifdef LSB_BWD_TRACE
+extern "C" LSB_API int lsb_bwd_trace_read(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, fa_bwd::g_bwd_trace, sizeof(fa_bwd::g_bwd_trace));
+}
+#endif
 
 int attn_bwd_tc_device_error() {
   int e = 0;
