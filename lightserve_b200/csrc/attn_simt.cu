@@ -330,11 +330,66 @@ __global__ void attn_dsum_rows_kernel(const T* __restrict__ o, const T* __restri
   if (lane == 0) dsum[warp] = acc;
 }
 
+// Vectorised Dsum for unit d-stride, 16-byte aligned rows: LPR lanes read one
+// row with 16-byte loads; 32 / LPR rows per warp.
+template <typename T, int LPR>
+__global__ void __launch_bounds__(256)
+attn_dsum_vec_kernel(const T* __restrict__ o, const T* __restrict__ dout, float* __restrict__ dsum,
+                     int H, int N, Strides4 so, Strides4 sdo, int64_t rows) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LPR;
+  const int sub = threadIdx.x % LPR;
+  const bool ok = row < rows;
+  float acc = 0.f;
+  if (ok) {
+    const int bh = (int)(row / N), m = (int)(row % N);
+    const int b = bh / H, h = bh % H;
+    Vec16<T> a = ld_vec16_stream(o + b * so.b + h * so.h + m * so.n + sub * VEC);
+    Vec16<T> c = ld_vec16_stream(dout + b * sdo.b + h * sdo.h + m * sdo.n + sub * VEC);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc = fmaf(to_f(a.v[j]), to_f(c.v[j]), acc);
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (ok && sub == 0) dsum[row] = acc;
+}
+
+// Vectorised dQ cast for a dense [B,H,N,D] output: 8 fp32 -> 8 x 16-bit per thread.
+template <typename T>
+__global__ void attn_dq_cast_vec_kernel(const float4* __restrict__ src, uint4* __restrict__ dst,
+                                        int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldcs(src + 2 * i), b = __ldcs(src + 2 * i + 1);
+    Vec16<T> v;
+    v.v[0] = from_f<T>(a.x); v.v[1] = from_f<T>(a.y); v.v[2] = from_f<T>(a.z); v.v[3] = from_f<T>(a.w);
+    v.v[4] = from_f<T>(b.x); v.v[5] = from_f<T>(b.y); v.v[6] = from_f<T>(b.z); v.v[7] = from_f<T>(b.w);
+    __stcs(dst + i, *reinterpret_cast<uint4*>(&v));
+  }
+}
+
 template <typename T>
 int launch_dsum(const void* o, const void* dout, float* dsum, int64_t B, int64_t H, int64_t N,
                 int64_t D, Strides4 so, Strides4 sdo, cudaStream_t st) {
   const int64_t rows = B * H * N;
   const int threads = 256;
+  constexpr int VEC = 16 / sizeof(T);
+  const bool vec = so.d == 1 && sdo.d == 1 && aligned16(o) && aligned16(dout) &&
+                   (so.n * sizeof(T)) % 16 == 0 && (so.h * sizeof(T)) % 16 == 0 &&
+                   (so.b * sizeof(T)) % 16 == 0 && (sdo.n * sizeof(T)) % 16 == 0 &&
+                   (sdo.h * sizeof(T)) % 16 == 0 && (sdo.b * sizeof(T)) % 16 == 0;
+  if (vec && (D == 16 * VEC || D == 8 * VEC)) {
+    const int lpr = (int)(D / VEC);
+    const int64_t blocks = (rows * lpr + threads - 1) / threads;
+    if (lpr == 16)
+      attn_dsum_vec_kernel<T, 16><<<(unsigned)blocks, threads, 0, st>>>(
+          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows);
+    else
+      attn_dsum_vec_kernel<T, 8><<<(unsigned)blocks, threads, 0, st>>>(
+          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows);
+    LSB_CHECK_LAUNCH("attn_bwd_dsum");
+    return LSB_OK;
+  }
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
   attn_dsum_rows_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(
       (const T*)o, (const T*)dout, dsum, (int)H, (int)N, (int)D, so, sdo, rows);
@@ -346,6 +401,17 @@ template <typename T>
 int launch_dq_cast(const float* dq_acc, void* dq, int64_t B, int64_t H, int64_t N, int64_t D,
                    Strides4 sdq, cudaStream_t st) {
   const int64_t total = B * H * N * D;
+  const bool dense = sdq.d == 1 && sdq.n == D && sdq.h == N * D && sdq.b == H * N * D;
+  if (sizeof(T) == 2 && dense && total % 8 == 0 && aligned16(dq) && aligned16(dq_acc)) {
+    const int64_t n8 = total / 8;
+    int64_t blocks = (n8 + 255) / 256;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    attn_dq_cast_vec_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(
+        reinterpret_cast<const float4*>(dq_acc), reinterpret_cast<uint4*>(dq), n8);
+    LSB_CHECK_LAUNCH("attn_dq_cast");
+    return LSB_OK;
+  }
   int64_t blocks = (total + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 16;
   if (blocks > cap) blocks = cap;
