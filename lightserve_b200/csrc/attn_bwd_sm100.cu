@@ -55,18 +55,23 @@ constexpr int KC = D / 64;
 
 constexpr int K_OFF = 0;
 constexpr int V_OFF = K_OFF + KC * KV_CHUNK;
-constexpr int Q_OFF = V_OFF + KC * KV_CHUNK;          // [2 stages][KC] Q chunks
-constexpr int DO_OFF = Q_OFF + 2 * KC * Q_CHUNK;      // [2 stages][KC] dO chunks
-constexpr int DS_OFF = DO_OFF + 2 * KC * Q_CHUNK;     // dS^T [128 keys][64 q] swizzled
-constexpr int RED_OFF = DS_OFF + BN * BM * 2;         // dQ staging [2 bufs][64 q][D] fp32
-constexpr int STAT_OFF = RED_OFF + 2 * BM * D * 4;    // [2][2][64] floats: lse2, dsum
-constexpr int BAR_OFF = STAT_OFF + 2 * 2 * BM * 4;
-constexpr int NBAR = 1 + 2 + 2 + 8 + 2 + 4;
+constexpr int NQS = 3;    // Q / dO / statistics ring stages
+constexpr int Q_OFF = V_OFF + KC * KV_CHUNK;          // [NQS][KC] Q chunks
+constexpr int DO_OFF = Q_OFF + NQS * KC * Q_CHUNK;    // [NQS][KC] dO chunks
+constexpr int DS_OFF = DO_OFF + NQS * KC * Q_CHUNK;   // dS^T [2][128 keys][64 q] swizzled
+constexpr int DS_BYTES = BN * BM * 2;
+constexpr int RED_OFF = DS_OFF + 2 * DS_BYTES;        // dQ staging [64 q][D] fp32
+constexpr int STAT_OFF = RED_OFF + BM * D * 4;        // [NQS][2][64] floats: lse2, dsum
+constexpr int BAR_OFF = STAT_OFF + NQS * 2 * BM * 4;
+// kv_full, q_full[NQS], q_empty[NQS], s_ready[2], dp_ready, p_ready[2], ds_ready,
+// dv_done, dk_done, dq_ready, dq_free, stat_full[NQS], red_full, red_free
+constexpr int NBAR = 1 + 3 * NQS + 2 + 1 + 2 + 7;
 constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
 constexpr int SMEM = SLOT_OFF + 16 + 1024;
+static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KiB shared-memory limit");
 
-// TMEM columns
-constexpr uint32_t T_S = 0, T_DP = 64, T_DV = 128, T_DK = 256, T_DQ = 384;
+// TMEM columns: S^T double-buffered (tile it uses T_S + (it & 1) * 64).
+constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 192, T_DK = 320, T_DQ = 448;
 
 struct Params {
   const float* lse;
@@ -115,20 +120,20 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;
-  uint64_t* q_empty = bars + 3;
-  uint64_t* s_ready = bars + 5;
-  uint64_t* dp_ready = bars + 6;
-  uint64_t* p_ready = bars + 7;
-  uint64_t* ds_ready = bars + 8;
-  uint64_t* dv_done = bars + 9;
-  uint64_t* dk_done = bars + 10;
-  uint64_t* dq_ready = bars + 11;
-  uint64_t* dq_free = bars + 12;
-  uint64_t* stat_full = bars + 13;  // [2]: per-stage log-sum-exp / Dsum staged
-  float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [2][lse2 64 | dsum 64]
-  uint64_t* red_full = bars + 15;  // [2 bufs]: dQ tile staged (256 arrivals)
-  uint64_t* red_free = bars + 17;  // [2 bufs]: its bulk reduction has read it
+  uint64_t* q_full = bars + 1;                 // [NQS]
+  uint64_t* q_empty = q_full + NQS;            // [NQS]
+  uint64_t* s_ready = q_empty + NQS;           // [2]: per S^T buffer
+  uint64_t* dp_ready = s_ready + 2;
+  uint64_t* p_ready = dp_ready + 1;            // [2]: per S^T buffer
+  uint64_t* ds_ready = p_ready + 2;
+  uint64_t* dv_done = ds_ready + 1;
+  uint64_t* dk_done = dv_done + 1;
+  uint64_t* dq_ready = dk_done + 1;
+  uint64_t* dq_free = dq_ready + 1;
+  uint64_t* stat_full = dq_free + 1;           // [NQS]: log-sum-exp / Dsum staged
+  uint64_t* red_full = stat_full + NQS;        // dQ tile staged (256 arrivals)
+  uint64_t* red_free = red_full + 1;           // its bulk reduction has read it
+  float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [NQS][lse2 64 | dsum 64]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SLOT_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,18 +147,20 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) { mbar_init(&q_full[s], 1); mbar_init(&q_empty[s], 1); }
-    mbar_init(s_ready, 1);
+    for (int s = 0; s < NQS; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+      mbar_init(&stat_full[s], 32);
+    }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s_ready[i], 1); mbar_init(&p_ready[i], 256); }
     mbar_init(dp_ready, 1);
-    mbar_init(p_ready, 256);
     mbar_init(ds_ready, 256);
     mbar_init(dv_done, 1);
     mbar_init(dk_done, 1);
     mbar_init(dq_ready, 1);
     mbar_init(dq_free, 256);
-    mbar_init(&stat_full[0], 32);
-    mbar_init(&stat_full[1], 32);
-    for (int i = 0; i < 2; ++i) { mbar_init(&red_full[i], 256); mbar_init(&red_free[i], 1); }
+    mbar_init(red_full, 256);
+    mbar_init(red_free, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -185,10 +192,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       }
     }
     for (int it = 0; it < n; ++it) {
-      const int s = it & 1;
-      // Stage s is reused once the MMAs of tile it-2 (and so every read of
+      const int s = it % NQS;
+      // Stage s is reused once the MMAs of tile it-NQS (and so every read of
       // its statistics, which precede ds_ready) have completed.
-      if (it >= 2 && !mbar_wait_warp(&q_empty[s], ((it >> 1) - 1) & 1, 0x501)) break;
+      if (it >= NQS && !mbar_wait_warp(&q_empty[s], ((it / NQS) - 1) & 1, 0x501)) break;
       const int m0 = (i0 + it) * BM;
       if (lane == 0) {
         mbar_arrive_expect_tx(&q_full[s], 2 * KC * Q_CHUNK);
@@ -239,38 +246,45 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
                  (acc || kk > 0) ? 1u : 0u);
         }
       };
+      // S^T is double-buffered in TMEM, so S^T(it+2) is issued as soon as
+      // dV(it) has read P^T(it) from the same buffer; the conversion
+      // warpgroups never wait for the MMA chain of the previous tile.
+      auto issue_s = [&](int jt) {
+        issue_t(T_S + (jt & 1) * 64, k_base, q_base + (jt % NQS) * KC * Q_CHUNK);
+        mma_commit(&s_ready[jt & 1]);
+        BWD_TRACE(true, 1, jt);
+      };
       bool ok = mbar_wait(kv_full, 0, 0x601) && mbar_wait(&q_full[0], 0, 0x602);
       if (ok) {
         tc_fence_after();
-        issue_t(T_S, k_base, q_base);
-        mma_commit(s_ready);
-        BWD_TRACE(true, 1, 0);
+        issue_s(0);
         issue_t(T_DP, v_base, do_base);
         mma_commit(dp_ready);
+        if (n > 1) {
+          ok = mbar_wait(&q_full[1], 0, 0x609);
+          tc_fence_after();
+          if (ok) issue_s(1);
+        }
       }
       for (int it = 0; ok && it < n; ++it) {
-        const int s = it & 1;
+        const int s = it % NQS;
         const uint32_t ph = it & 1;
-        if (!mbar_wait(p_ready, ph, 0x603)) { ok = false; break; }
+        if (!mbar_wait(&p_ready[it & 1], (it >> 1) & 1, 0x603)) { ok = false; break; }
         BWD_TRACE(true, 2, it);
         tc_fence_after();
-        issue_acc(T_DV, T_S, do_base + s * KC * Q_CHUNK, it > 0);
+        issue_acc(T_DV, T_S + (it & 1) * 64, do_base + s * KC * Q_CHUNK, it > 0);
         mma_commit(dv_done);
         BWD_TRACE(true, 3, it);
-        if (it + 1 < n) {
-          const int s1 = (it + 1) & 1;
-          // S^T(it+1) overwrites P^T(it): wait until dV(it) has read it.
-          if (!mbar_wait(&q_full[s1], ((it + 1) >> 1) & 1, 0x604) ||
-              !mbar_wait(dv_done, ph, 0x605)) { ok = false; break; }
-          tc_fence_after();
-          issue_t(T_S, k_base, q_base + s1 * KC * Q_CHUNK);
-          mma_commit(s_ready);
-          BWD_TRACE(true, 1, it + 1);
-        }
         if (!mbar_wait(ds_ready, ph, 0x606)) { ok = false; break; }
         BWD_TRACE(true, 4, it);
         tc_fence_after();
-        issue_acc(T_DK, T_DP, q_base + s * KC * Q_CHUNK, it > 0);
+        if (it + 1 < n) {
+          // dS^T(it) lives in S buffer it & 1, so dP^T(it+1) may overwrite
+          // dP^T(it) as soon as both warpgroups have read it (ds_ready).
+          issue_t(T_DP, v_base, do_base + ((it + 1) % NQS) * KC * Q_CHUNK);
+          mma_commit(dp_ready);
+        }
+        issue_acc(T_DK, T_S + (it & 1) * 64 + 16, q_base + s * KC * Q_CHUNK, it > 0);
         mma_commit(dk_done);
         BWD_TRACE(true, 5, it);
         if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x607)) { ok = false; break; }
@@ -278,40 +292,38 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t a = smem_desc_sw128(k_base + kk * 2048, KV_CHUNK, 1024);
-          const uint64_t bd = smem_desc_sw128(ds_base + kk * 2048, BN * BM * 2, 1024);
+          const uint64_t bd = smem_desc_sw128(ds_base + (it & 1) * DS_BYTES + kk * 2048, DS_BYTES, 1024);
           mma_ss(tmem + T_DQ, a, bd, ID_DQ, kk > 0);
         }
         mma_commit(dq_ready);
         BWD_TRACE(true, 6, it);
         mma_commit(&q_empty[s]);
-        if (it + 1 < n) {
-          const int s1 = (it + 1) & 1;
-          // dP^T(it+1) overwrites dS^T(it): wait until dK(it) has read it.
-          if (!mbar_wait(dk_done, ph, 0x608)) { ok = false; break; }
+        if (it + 2 < n) {
+          // S^T(it+2) overwrites P^T(it) and dS^T(it) in buffer it & 1:
+          // dV(it) and dK(it) must have read them.
+          if (!mbar_wait(&q_full[(it + 2) % NQS], ((it + 2) / NQS) & 1, 0x604) ||
+              !mbar_wait(dk_done, ph, 0x605)) { ok = false; break; }
           tc_fence_after();
-          issue_t(T_DP, v_base, do_base + s1 * KC * Q_CHUNK);
-          mma_commit(dp_ready);
+          issue_s(it + 2);
         }
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------- dQ reducer --
     // Adds each staged 64-row dQ tile into the fp32 dQ buffer (rows are
-    // contiguous there) with one bulk reduction; two staging buffers let the
-    // next tile be staged while this one is being read.
+    // contiguous there) with one bulk reduction. Tiles are staged one tile
+    // late, so the staging buffer is normally read by the time it is reused.
     reg_dealloc<72>();
     if (lane == 0) {
       for (int it = 0; it < n; ++it) {
-        const int bsel = it & 1;
-        if (!mbar_wait(&red_full[bsel], (it >> 1) & 1, 0x901)) break;
+        if (!mbar_wait(red_full, it & 1, 0x901)) break;
         const int m0 = (i0 + it) * BM;
         const int rows = min(BM, p.N - m0);
         bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + m0) * D,
-                            reinterpret_cast<const float*>(smem + RED_OFF) + bsel * BM * D,
-                            rows * D * 4);
+                            reinterpret_cast<const float*>(smem + RED_OFF), rows * D * 4);
         bulk_commit();
-        bulk_wait_read_1();  // the previous tile's reduction has read its buffer
-        if (it > 0) mbar_arrive(&red_free[bsel ^ 1]);
+        bulk_wait_read();  // the staging tile may be rewritten once this has read it
+        mbar_arrive(red_free);
       }
       bulk_wait_all();  // every reduction has landed before the CTA exits
     }
@@ -342,13 +354,12 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(dq_free);
-      const int bsel = jt & 1;
-      if (jt >= 2 && !mbar_wait_warp(&red_free[bsel], ((jt >> 1) - 1) & 1, 0x802)) return false;
-      float* stage = reinterpret_cast<float*>(smem + RED_OFF) + bsel * BM * D + half * 32 * D;
+      if (jt >= 1 && !mbar_wait_warp(red_free, (jt - 1) & 1, 0x802)) return false;
+      float* stage = reinterpret_cast<float*>(smem + RED_OFF) + half * 32 * D;
 #pragma unroll
       for (int c = 0; c < 32; ++c) stage[c * D + r] = __uint_as_float(qv[c]) * p.scale;
       fence_proxy_async_smem();
-      mbar_arrive(&red_full[bsel]);
+      mbar_arrive(red_full);
       BWD_TRACE(r == 0 && half == 0, 12, jt);
       return true;
     };
@@ -356,13 +367,14 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     for (int it = 0; it < n; ++it) {
       const uint32_t ph = it & 1;
       const int m0 = (i0 + it) * BM;
-      const float* st = stats + (it & 1) * 2 * BM;
-      if (!mbar_wait_warp(&stat_full[it & 1], (it >> 1) & 1, 0x705)) { ok = false; break; }
-      if (!mbar_wait_warp(s_ready, ph, 0x701)) { ok = false; break; }
+      const float* st = stats + (it % NQS) * 2 * BM;
+      const uint32_t sbuf = T_S + (it & 1) * 64;
+      if (!mbar_wait_warp(&stat_full[it % NQS], (it / NQS) & 1, 0x705)) { ok = false; break; }
+      if (!mbar_wait_warp(&s_ready[it & 1], (it >> 1) & 1, 0x701)) { ok = false; break; }
       BWD_TRACE(r == 0 && half == 0, 7, it);
       tc_fence_after();
       uint32_t sv[32];
-      tmem_ld32(lane_addr + T_S + cb, sv);
+      tmem_ld32(lane_addr + sbuf + cb, sv);
       tmem_ld_wait();
       // Masks: causal (q < key), and rows/columns past the sequence end.
       const bool need_mask = (m0 + BM > p.N) || (kv0 + BN > p.N) || (p.causal && m0 < kv0 + BN);
@@ -384,13 +396,11 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         pf[2 * cc + 1] = p1;
         pk[cc] = pack2<FMT>(p0, p1);
       }
-      tmem_st16(lane_addr + T_S + half * 32, pk);
+      tmem_st16(lane_addr + sbuf + half * 32, pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_ready);
+      mbar_arrive(&p_ready[it & 1]);
       BWD_TRACE(r == 0 && half == 0, 8, it);
-      // The previous tile's dQ^T (ready by now) is staged while dP^T(it) finishes.
-      if (it > 0 && !stage_dq(it - 1)) { ok = false; break; }
 
       if (!mbar_wait_warp(dp_ready, ph, 0x702)) { ok = false; break; }
       BWD_TRACE(r == 0 && half == 0, 9, it);
@@ -404,13 +414,13 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         dsk[cc] = pack2<FMT>(pf[2 * cc] * (__uint_as_float(sv[2 * cc]) - ds2.x),
                              pf[2 * cc + 1] * (__uint_as_float(sv[2 * cc + 1]) - ds2.y));
       }
-      tmem_st16(lane_addr + T_DP + half * 32, dsk);
+      tmem_st16(lane_addr + sbuf + half * 32 + 16, dsk);  // beside P^T, in the S buffer
       // dS^T row half -> shared (128-byte swizzle) for the dQ^T GEMM, once the
       // previous dQ^T GEMM has finished reading the buffer.
-      // (dQ^T(it-1) has completed -- stage_dq waited for it -- so the dQ GEMM
-      // no longer reads the dS^T buffer.)
+      // dS^T buffer it & 1 was last read by dQ^T(it-2), which stage_dq(it-2)
+      // waited for during the previous tile.
       {
-        uint8_t* rowp = sDS + r * 128;
+        uint8_t* rowp = sDS + (it & 1) * DS_BYTES + r * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int chunk = half * 4 + c;
@@ -423,6 +433,9 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       tc_fence_before();
       mbar_arrive(ds_ready);
       BWD_TRACE(r == 0 && half == 0, 10, it);
+      // The previous tile's dQ^T (complete by now) is staged while dK(it) and
+      // dQ^T(it) run on the tensor cores.
+      if (it > 0 && !stage_dq(it - 1)) { ok = false; break; }
 
     }
     if (ok && !stage_dq(n - 1)) ok = false;
