@@ -148,6 +148,27 @@ LSB_API int lsb_paged_decode(const void* q, const void* k_cache, const void* v_c
                      void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Fused RoPE + paged KV-cache write for one decode step (one token per
+ * sequence). Replaces the decode-time use of lightserve's apply_rope
+ * (model/minimal_llama.py:167-182: q*cos + rotate_half(q)*sin with each
+ * product and the sum rounded to the model dtype) plus the cache write and
+ * slot lookup through the block table (engine/block_manager.py:58-61).
+ * qkv: [S, 3, H, D] with strides {s_s, s_part, s_h} (d contiguous);
+ * cos/sin tables: [max_pos, D] with row stride s_pos; positions: int64 [S];
+ * block_tables: int32 [S, max_blocks_per_seq]. Writes rotated q to q_out
+ * [S, H, D] contiguous, rotated k and raw v into the caches at slot
+ * (block_tables[s][pos / block_size], pos % block_size), and
+ * context_lens[s] = pos + 1 when context_lens != NULL.
+ */
+LSB_API int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                              const void* cos_table, const void* sin_table, int64_t s_pos,
+                              const int64_t* positions, const int32_t* block_tables,
+                              int64_t max_blocks_per_seq, void* q_out, void* k_cache,
+                              void* v_cache, int32_t* context_lens, int64_t S, int64_t H,
+                              int64_t D, int64_t num_blocks, int64_t block_size, int dtype,
+                              void* stream);
+
+/*
  * Allocation-free paged decode. No counterpart exists in lightserve: this is
  * lsb_paged_decode for callers that cannot allocate device memory (runtimes
  * whose own pool owns the GPU's memory, FFI bindings without access to the

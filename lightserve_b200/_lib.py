@@ -6,6 +6,7 @@ CPU fallback behind these functions.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -54,6 +55,8 @@ SIGNATURES = {
     "lsb_paged_decode_workspace_size": (_I64, [_I64, _I64, _I64, _I64, _I64]),
     "lsb_paged_decode": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                               _I64, _I64, _I64, _I64, _F, _I, _P, _I64, _P]),
+    "lsb_rope_kv_write": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P,
+                               _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_paged_decode_static_scratch_capacity": (_I64, []),
     "lsb_paged_decode_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                              _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
@@ -114,6 +117,16 @@ def strides4(t: torch.Tensor):
 
 def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+_NULL = contextlib.nullcontext()
+
+
+def device_guard(device: torch.device):
+    """Makes `device` current for the launch; free when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NULL
+    return torch.cuda.device(device)
 
 
 def stream_ptr(device: torch.device | None = None) -> int:

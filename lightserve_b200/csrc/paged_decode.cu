@@ -642,3 +642,93 @@ extern "C" int lsb_paged_decode_static_scratch(
                           max_blocks_per_seq, block_size, num_blocks, sq_s, sq_h, so_s, so_h,
                           scale, dtype, ws, need, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Fused RoPE + paged KV-cache write for one decode step.
+//
+// Replaces, for the decode runner, the eager sequence of lightserve's
+// apply_rope (model/minimal_llama.py:167-182: q*cos + rotate_half(q)*sin,
+// each product and the sum rounded to the model dtype, as torch computes it)
+// followed by the cache write, the block-table slot lookup
+// (engine/block_manager.py:58-61) and the context-length update.
+// One CTA per sequence; threads walk (head, rotation pair).
+namespace lsb {
+
+template <typename T>
+__global__ void rope_kv_write_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part,
+                                     int64_t s_h, const T* __restrict__ cos_t,
+                                     const T* __restrict__ sin_t, int64_t s_pos,
+                                     const int64_t* __restrict__ positions,
+                                     const int32_t* __restrict__ block_tables, int max_blocks,
+                                     T* __restrict__ q_out, T* __restrict__ k_cache,
+                                     T* __restrict__ v_cache, int32_t* __restrict__ context_lens,
+                                     int H, int D, int num_blocks, int bs) {
+  const int s = blockIdx.x;
+  const int64_t pos = positions[s];
+  const int half = D / 2;
+  const int64_t bidx = pos / bs;
+  const int blk = (bidx >= 0 && bidx < max_blocks) ? block_tables[(int64_t)s * max_blocks + bidx] : -1;
+  const bool write = blk >= 0 && blk < num_blocks;
+  if (threadIdx.x == 0 && context_lens != nullptr) context_lens[s] = (int32_t)(pos + 1);
+  const T* cs = cos_t + pos * s_pos;
+  const T* sn = sin_t + pos * s_pos;
+  const T* qrow = qkv + s * s_s;
+  for (int idx = threadIdx.x; idx < H * half; idx += blockDim.x) {
+    const int h = idx / half, i = idx % half;
+    const float c0 = to_f(cs[i]), c1 = to_f(cs[i + half]);
+    const float n0 = to_f(sn[i]), n1 = to_f(sn[i + half]);
+    // rotate_half(x) = [-x2, x1]; every product and sum rounded to T.
+    auto rope = [&](float x1, float x2, T& o1, T& o2) {
+      const float a = to_f(from_f<T>(__fmul_rn(x1, c0)));
+      const float b = to_f(from_f<T>(__fmul_rn(-x2, n0)));
+      o1 = from_f<T>(__fadd_rn(a, b));
+      const float c = to_f(from_f<T>(__fmul_rn(x2, c1)));
+      const float d = to_f(from_f<T>(__fmul_rn(x1, n1)));
+      o2 = from_f<T>(__fadd_rn(c, d));
+    };
+    const T* qh = qrow + h * s_h;
+    const T* kh = qrow + s_part + h * s_h;
+    const T* vh = qrow + 2 * s_part + h * s_h;
+    T o1, o2;
+    rope(to_f(qh[i]), to_f(qh[i + half]), o1, o2);
+    T* qo = q_out + ((int64_t)s * H + h) * D;
+    qo[i] = o1;
+    qo[i + half] = o2;
+    if (write) {
+      const int64_t dst = (((int64_t)blk * H + h) * bs + (pos % bs)) * D;
+      rope(to_f(kh[i]), to_f(kh[i + half]), o1, o2);
+      k_cache[dst + i] = o1;
+      k_cache[dst + i + half] = o2;
+      v_cache[dst + i] = vh[i];
+      v_cache[dst + i + half] = vh[i + half];
+    }
+  }
+}
+
+}  // namespace lsb
+
+extern "C" int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                                 const void* cos_table, const void* sin_table, int64_t s_pos,
+                                 const int64_t* positions, const int32_t* block_tables,
+                                 int64_t max_blocks_per_seq, void* q_out, void* k_cache,
+                                 void* v_cache, int32_t* context_lens, int64_t S, int64_t H,
+                                 int64_t D, int64_t num_blocks, int64_t block_size, int dtype,
+                                 void* stream) {
+  LSB_CHECK_ARG(S >= 0 && H > 0 && D > 0 && (D % 2) == 0 && num_blocks > 0 && block_size > 0 &&
+                    max_blocks_per_seq > 0,
+                "rope_kv_write: bad sizes");
+  if (S == 0) return LSB_OK;
+  LSB_CHECK_ARG(qkv && cos_table && sin_table && positions && block_tables && q_out && k_cache &&
+                    v_cache,
+                "rope_kv_write: null pointer");
+  LSB_CHECK_ARG(S <= 0x7fffffff, "rope_kv_write: S too large");
+  cudaStream_t st = (cudaStream_t)stream;
+  return LSB_DISPATCH_DTYPE(dtype, T, [&] {
+    lsb::rope_kv_write_kernel<T><<<(unsigned)S, 256, 0, st>>>(
+        (const T*)qkv, s_s, s_part, s_h, (const T*)cos_table, (const T*)sin_table, s_pos,
+        positions, block_tables, (int)max_blocks_per_seq, (T*)q_out, (T*)k_cache, (T*)v_cache,
+        context_lens, (int)H, (int)D, (int)num_blocks, (int)block_size);
+    LSB_CHECK_LAUNCH("rope_kv_write");
+    return LSB_OK;
+  });
+}

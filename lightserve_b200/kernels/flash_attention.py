@@ -37,7 +37,7 @@ def _check_qkv(q, k, v):
 def _attn_fwd(q, k, v, o, lse, causal: bool, impl: int = _lib.IMPL_AUTO):
     B, H, N, D = q.shape
     lib = _lib.load()
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.lsb_attn_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), _lib.ptr(lse),
             B, H, N, D, _lib.strides4(q), _lib.strides4(k), _lib.strides4(v), _lib.strides4(o),

@@ -47,7 +47,7 @@ def _flash_attention_backward(do: torch.Tensor, q: torch.Tensor, k: torch.Tensor
     lib = _lib.load()
     ws_bytes = lib.lsb_attn_bwd_workspace_size(B, H, N, D)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.lsb_attn_bwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), L.data_ptr(),
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, H, N, D,

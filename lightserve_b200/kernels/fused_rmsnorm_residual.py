@@ -43,7 +43,7 @@ def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Ten
         return t.stride(0) if M > 1 else N
 
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.device_guard(x.device):
         rc = lib.lsb_rmsnorm_residual(
             x.data_ptr(), residual.data_ptr(), weight.data_ptr(), out.data_ptr(),
             residual_out.data_ptr(), M, N, ld(x), ld(residual), ld(out), ld(residual_out), float(eps), _lib.dtype_code(x.dtype), _lib.stream_ptr(x.device),

@@ -35,7 +35,7 @@ def write_kv_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_ca
     assert k.stride(2) == 1 and v.stride(2) == 1, "k/v must be contiguous along D"
     assert slot_mapping.dtype == torch.int64 and slot_mapping.shape == (T,) and slot_mapping.is_contiguous()
     lib = _lib.load()
-    with torch.cuda.device(k.device):
+    with _lib.device_guard(k.device):
         rc = lib.lsb_kv_cache_write(
             k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), slot_mapping.data_ptr(),
             T, H, D, nb, bs, k.stride(0), k.stride(1), v.stride(0), v.stride(1),
@@ -87,7 +87,7 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
     assert workspace.numel() * workspace.element_size() >= need, "workspace too small"
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.lsb_paged_decode(
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(),
             context_lens.data_ptr(), out.data_ptr(), S, H, D, max_blocks, bs, nb,
@@ -97,3 +97,39 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
         )
     _lib.check(rc, "lsb_paged_decode")
     return out
+
+
+def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, positions: torch.Tensor,
+                  block_tables: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, context_lens: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step's RoPE + KV-cache write, fused.
+
+    qkv: [S, 3, H, D] (the fused QKV projection); cos/sin: [max_pos, D] tables in
+    the model dtype; positions: int64 [S] (position of each sequence's new token);
+    block_tables: int32 [S, max_blocks]. Writes rotated q into q_out [S, H, D],
+    rotated k and v into the caches at the token's slot, and context_lens[s] =
+    positions[s] + 1 when given. Rounding matches lightserve's apply_rope
+    (model/minimal_llama.py:167-182) computed with torch ops in the model dtype.
+    """
+    assert qkv.ndim == 4 and qkv.shape[1] == 3 and qkv.stride(3) == 1, "qkv must be [S, 3, H, D]"
+    S, _, H, D = qkv.shape
+    assert k_cache.ndim == 4 and k_cache.shape == v_cache.shape and k_cache.is_contiguous()
+    nb, Hc, bs, Dc = k_cache.shape
+    assert (Hc, Dc) == (H, D)
+    assert cos.shape == sin.shape and cos.shape[1] == D and cos.stride() == sin.stride() and cos.stride(1) == 1
+    assert qkv.dtype == cos.dtype == sin.dtype == k_cache.dtype == q_out.dtype
+    assert q_out.shape == (S, H, D) and q_out.is_contiguous()
+    assert positions.dtype == torch.int64 and positions.shape == (S,) and positions.is_contiguous()
+    assert block_tables.dtype == torch.int32 and block_tables.is_contiguous() and block_tables.shape[0] == S
+    if context_lens is not None:
+        assert context_lens.dtype == torch.int32 and context_lens.shape == (S,) and context_lens.is_contiguous()
+    lib = _lib.load()
+    with _lib.device_guard(qkv.device):
+        rc = lib.lsb_rope_kv_write(
+            qkv.data_ptr(), qkv.stride(0), qkv.stride(1), qkv.stride(2), cos.data_ptr(), sin.data_ptr(),
+            cos.stride(0), positions.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],
+            q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), _lib.ptr(context_lens),
+            S, H, D, nb, bs, _lib.dtype_code(qkv.dtype), _lib.stream_ptr(qkv.device),
+        )
+    _lib.check(rc, "lsb_rope_kv_write")
+    return q_out

@@ -11,7 +11,8 @@ side-stream warm-up before capture (``:129-135``), one captured step
 logits (``:114-118``).
 
 Per step and layer: fused add+RMSNorm (lsb kernel) -> fused QKV GEMM (cuBLAS)
--> RoPE at each sequence's position -> ``write_kv_cache`` (lsb kernel) ->
+-> ``rope_kv_write`` (lsb kernel: RoPE at each sequence's position, K/V into
+the cache slot from the block table, context lengths) ->
 ``paged_decode_attention`` (lsb kernel) -> O projection -> add+RMSNorm ->
 SwiGLU MLP. All buffers are static, so a step is graph-capturable.
 
@@ -30,8 +31,8 @@ import torch.nn.functional as F
 from ..engine import BlockManager, Request
 from ..kernels.fused_rmsnorm_residual import fused_add_rmsnorm
 from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
-                                        write_kv_cache)
-from .minimal_llama import LlamaConfig, LlamaWeights, apply_rope, llama_forward, precompute_rope
+                                        rope_kv_write, write_kv_cache)
+from .minimal_llama import LlamaConfig, LlamaWeights, llama_forward, precompute_rope
 
 
 class PagedKVCache:
@@ -82,6 +83,7 @@ class PagedDecoder:
         self.block_tables = torch.full((S, max_blocks_per_seq), -1, dtype=torch.int32, device=dev)
         self.zeros = torch.zeros(S, Hd, dtype=config.dtype, device=dev)
         self.attn_out = torch.empty(S, H, D, dtype=config.dtype, device=dev)
+        self.q_rot = torch.empty(S, H, D, dtype=config.dtype, device=dev)
         self.ws = paged_decode_workspace((S, H, D), max_blocks_per_seq, cache.block_size, dev)
         self.graph = None
         self.requests: list = []
@@ -133,19 +135,16 @@ class PagedDecoder:
         cfg, S, bs = self.cfg, self.S, self.cache.block_size
         H, D, Hd, I = cfg.n_heads, cfg.head_dim, cfg.hidden_size, cfg.intermediate_size
         pos = self.positions
-        self.context_lens.copy_(pos + 1)
-        blk = torch.gather(self.block_tables, 1, (pos // bs).unsqueeze(1)).squeeze(1).to(torch.int64)
-        slots = blk * bs + pos % bs
-        cos = self.cos[pos].unsqueeze(1)
-        sin = self.sin[pos].unsqueeze(1)
         residual = F.embedding(self.tokens, self.w.embed_tokens)
         x = self.zeros
         for li, layer in enumerate(self.w.layers):
             fz = self.fused[li]
             normed, residual = fused_add_rmsnorm(x, residual, layer.input_layernorm_weight, eps=cfg.rms_eps)
             qkv = (normed @ fz.w_qkv).view(S, 3, H, D)
-            q, k = apply_rope(qkv[:, 0], qkv[:, 1], cos, sin)
-            write_kv_cache(k, qkv[:, 2], self.cache.k[li], self.cache.v[li], slots)
+            # RoPE at each sequence's position + K/V into its cache slot, fused
+            # (also sets context_lens = positions + 1).
+            q = rope_kv_write(qkv, self.cos, self.sin, pos, self.block_tables, self.q_rot,
+                              self.cache.k[li], self.cache.v[li], self.context_lens)
             attn = paged_decode_attention(q, self.cache.k[li], self.cache.v[li], self.block_tables,
                                           self.context_lens, out=self.attn_out, workspace=self.ws)
             x = attn.view(S, Hd) @ layer.o_proj
