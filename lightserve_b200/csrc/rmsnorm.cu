@@ -34,8 +34,13 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nvec) {
+#ifdef LSB_RMS_PLAIN_LD
+      Vec16<T> a = ld_vec16(xr + c * VEC);
+      Vec16<T> b = ld_vec16(rr + c * VEC);
+#else
       Vec16<T> a = ld_vec16_stream(xr + c * VEC);
       Vec16<T> b = ld_vec16_stream(rr + c * VEC);
+#endif
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
         T h = from_f<T>(to_f(a.v[j]) + to_f(b.v[j]));
@@ -71,8 +76,13 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
 #pragma unroll
       for (int j = 0; j < VEC; ++j)
         ov.v[j] = from_f<T>(to_f(hv[i].v[j]) * rrms * to_f(wv.v[j]));
+#ifdef LSB_RMS_PLAIN_ST
+      *reinterpret_cast<uint4*>(hrow + c * VEC) = *reinterpret_cast<uint4*>(&hv[i]);
+      *reinterpret_cast<uint4*>(orow + c * VEC) = *reinterpret_cast<uint4*>(&ov);
+#else
       __stcs(reinterpret_cast<uint4*>(hrow + c * VEC), *reinterpret_cast<uint4*>(&hv[i]));
       __stcs(reinterpret_cast<uint4*>(orow + c * VEC), *reinterpret_cast<uint4*>(&ov));
+#endif
     }
   }
 }
@@ -126,7 +136,10 @@ static int launch_rmsnorm(const void* x, const void* r, const void* w, void* out
   if (vec_ok) {
     const int nvec = (int)(N / VEC);
     // Aim for ~4 vectors per thread, between 32 and 512 threads per row.
-    int threads = ((nvec + 3) / 4 + 31) / 32 * 32;
+#ifndef LSB_RMS_VPT
+#define LSB_RMS_VPT 2
+#endif
+    int threads = ((nvec + LSB_RMS_VPT - 1) / LSB_RMS_VPT + 31) / 32 * 32;
     threads = threads < 32 ? 32 : (threads > 512 ? 512 : threads);
     const int need = (nvec + threads - 1) / threads;
     const T* xp = (const T*)x; const T* rp = (const T*)r; const T* wp = (const T*)w;
