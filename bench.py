@@ -379,5 +379,15 @@ def main():
     print(json.dumps(line))
 
 
+def _shutdown():
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()
+
+
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    finally:
+        _shutdown()
