@@ -9,22 +9,33 @@
 // dQ += dS K * scale accumulated in an fp32 buffer, rounded at the end.
 //
 // B200 design: one CTA per 128 keys of one (batch, head), looping over query
-// tiles of 64 rows (causal: starting at the diagonal). Everything is computed
-// transposed so the 128 keys are the TMEM lanes:
-//   S^T  = K Q^T      (SS MMA)  -> TMEM cols [0,64)
-//   dP^T = V dO^T     (SS MMA)  -> TMEM cols [64,128)
-//   dV  += P^T dO     (TS MMA, P^T packed to 16 bits over S^T)  -> [128,256)
-//   dK  += dS^T Q     (TS MMA, dS^T packed over dP^T)           -> [256,384)
-//   dQ^T = K^T dS^T   (SS MMA, K^T read MN-major from the K tile, dS^T
-//                      from a 128-byte-swizzled shared tile)    -> [384,448)
-// Warp 0 streams K/V once and Q/dO tiles (plus each tile's log-sum-exp and
-// Dsum) through a 2-stage ring; warp 1 owns TMEM and issues the MMAs; warp 2
-// adds each finished 64-row dQ tile into the fp32 dQ buffer with one bulk
-// shared->global reduction (double-buffered staging). Warpgroups 1 and 2 split
-// every tile's 64 query columns: thread = key for P^T / dS^T, thread =
-// head-dim index when staging dQ^T; the previous tile's dQ^T is staged while
-// the current dP^T completes.
+// tiles of 128 rows (causal: starting at the diagonal). Every GEMM is issued
+// as M=128, N=128 tcgen05.mma instructions: a tcgen05.mma costs about the same
+// time for N=64 as for N=128, so 64-wide tiles would halve the tensor-core
+// throughput. Everything is computed transposed so the 128 keys are the TMEM
+// lanes; TMEM (512 columns) holds
+//   [0,128)   dV  += P^T dO    (TS MMA: P^T packed to 16 bits inside S^T)
+//   [128,256) dK  += dS^T Q    (TS MMA: dS^T packed inside S^T)
+//   [256,384) S^T  = K Q^T     (SS MMA), then P^T and dS^T in 16-bit pairs
+//   [384,512) dP^T = V dO^T    (SS MMA), then dQ^T = K^T dS^T (SS MMA, K^T
+//             read MN-major from the K tile, dS^T from a 128-byte-swizzled
+//             shared tile)
+// Warp 0 streams K/V once, Q tiles (plus each tile's log-sum-exp and Dsum)
+// through a 2-stage ring and dO tiles through one buffer (dO(i+1) loads
+// while dQ(i), dK(i) and S(i+1) run); warp 1 owns TMEM and issues the MMAs
+// in the order dV(i), dQ(i), dK(i), S(i+1), dP(i+1); warp 2 adds the finished
+// dQ tile into the fp32 dQ buffer with two bulk shared->global reductions.
+// Warpgroups 1 and 2 split every tile's 128 query columns (64 each): thread =
+// key for P^T / dS^T, thread = head-dim index for dQ^T. Once dQ^T(i) is in
+// registers, warpgroup 1 stages its 64 query rows in a dedicated 32 KiB
+// buffer and warpgroup 2 in the dS^T tile (free after dQ^T(i)). The fp32
+// reduction into L2 runs at about 21 B/clk per SM with every SM reducing,
+// so the 64 KiB of one tile takes ~3100 cycles: the reductions of tile i
+// overlap all of tile i+1's work, and only the next dS^T write waits for
+// the dS^T-tile half to have been read.
 // All mbarrier waits are bounded (sm100.cuh).
+#include <algorithm>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -46,41 +57,49 @@ namespace fa_bwd {
 using namespace sm100;
 
 constexpr int BN = 128;   // keys per CTA (TMEM lanes)
-constexpr int BM = 64;    // query rows per inner tile
+constexpr int BM = 128;   // query rows per inner tile
 constexpr int D = 128;    // head dim served by this kernel
 constexpr int THREADS = 384;
-constexpr int KV_CHUNK = 128 * 128;  // [128 rows][64 cols] 16-bit box
-constexpr int Q_CHUNK = 64 * 128;    // [64 rows][64 cols] 16-bit box
-constexpr int KC = D / 64;
+constexpr int CHUNK = 128 * 128;  // [128 rows][64 cols] 16-bit box, 128-byte swizzle
+constexpr int KC = D / 64;        // chunks per K, V, Q or dO tile
+constexpr int TILE = KC * CHUNK;  // 32 KiB
 
 constexpr int K_OFF = 0;
-constexpr int V_OFF = K_OFF + KC * KV_CHUNK;
-constexpr int NQS = 3;    // Q / dO / statistics ring stages
-constexpr int Q_OFF = V_OFF + KC * KV_CHUNK;          // [NQS][KC] Q chunks
-constexpr int DO_OFF = Q_OFF + NQS * KC * Q_CHUNK;    // [NQS][KC] dO chunks
-constexpr int DS_OFF = DO_OFF + NQS * KC * Q_CHUNK;   // dS^T [2][128 keys][64 q] swizzled
-constexpr int DS_BYTES = BN * BM * 2;
-constexpr int RED_OFF = DS_OFF + 2 * DS_BYTES;        // dQ staging [64 q][D] fp32
-constexpr int STAT_OFF = RED_OFF + BM * D * 4;        // [NQS][2][64] floats: lse2, dsum
+constexpr int V_OFF = K_OFF + TILE;
+constexpr int NQS = 2;    // Q / statistics ring stages
+constexpr int Q_OFF = V_OFF + TILE;             // [NQS] Q tiles
+constexpr int DO_OFF = Q_OFF + NQS * TILE;      // dO tile
+constexpr int DS_OFF = DO_OFF + TILE;           // dS^T [2 chunks][128 keys][64 q]; dQ staging 1
+constexpr int STG_OFF = DS_OFF + TILE;          // dQ staging 0
+constexpr int STAGE_ROWS = 64;                  // dQ rows per staging buffer (64 x D fp32 = 32 KiB)
+static_assert(STAGE_ROWS * D * 4 == TILE, "a dQ staging buffer holds half a query tile");
+constexpr int STAT_OFF = STG_OFF + TILE;        // [NQS][2][BM] floats: lse2, dsum
 constexpr int BAR_OFF = STAT_OFF + NQS * 2 * BM * 4;
-// kv_full, q_full[NQS], q_empty[NQS], s_ready[2], dp_ready, p_ready[2], ds_ready,
-// dv_done, dk_done, dq_ready, dq_free, stat_full[NQS], red_full, red_free
-constexpr int NBAR = 1 + 3 * NQS + 2 + 1 + 2 + 7;
+// kv_full, kv_empty, q_full[NQS], q_empty[NQS], stat_full[NQS], do_full, do_empty,
+// s_ready, p_ready, dp_ready, ds_ready, dq_ready, dq_free, dk_done, red_full[2],
+// red_free[2], item_full[NIS], item_empty[NIS]
+constexpr int NIS = 4;    // work-item id ring slots
+constexpr int NBAR = 2 + 3 * NQS + 13 + 2 * NIS;
 constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
-constexpr int SMEM = SLOT_OFF + 16 + 1024;
+constexpr int ITEM_OFF = SLOT_OFF + 16;         // [NIS] work-item ids
+constexpr int SMEM = ITEM_OFF + NIS * 4;
 static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KiB shared-memory limit");
 
-// TMEM columns: S^T double-buffered (tile it uses T_S + (it & 1) * 64).
-constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 192, T_DK = 320, T_DQ = 448;
+constexpr uint32_t T_DV = 0, T_DK = 128, T_S = 256, T_DP = 384;
+#ifndef LSB_BWD_GROUP
+#define LSB_BWD_GROUP 16
+#endif
+constexpr int BH_GROUP = LSB_BWD_GROUP;  // (batch, head) slices scheduled together
 
 struct Params {
   const float* lse;
   const float* dsum;
   float* dq_acc;
+  int* work_counter;  // zeroed before launch; CTAs take work items from it
   void* dk;
   void* dv;
   int64_t sdk_b, sdk_h, sdk_n, sdv_b, sdv_h, sdv_n;
-  int H, N;
+  int H, N, BH;
   float scale, scale_log2;
   int causal;
 };
@@ -88,21 +107,31 @@ struct Params {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void named_bar(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 #ifdef LSB_BWD_TRACE
-// Debug-build timeline of CTA (0, 0): clock64 per event and query tile.
+// Debug-build timeline of the first work item of CTA 0: clock64 per event and
+// query tile; per work item: global timer at start / first S^T / end, SM id, tiles.
 __device__ long long g_bwd_trace[16][64];
+__device__ unsigned long long g_bwd_cta[8192][5];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 #define BWD_TRACE(cond, ev, it)                                               \
   do {                                                                        \
-    if ((cond) && blockIdx.x == 0 && blockIdx.y == 0 && (it) < 64)            \
-      g_bwd_trace[ev][it] = clock64();                                        \
+    if ((cond) && blockIdx.x == 0 && (it) < 64) g_bwd_trace[ev][it] = clock64(); \
+  } while (0)
+#define BWD_ITEM(item, slot, val)                                             \
+  do {                                                                        \
+    if ((item) < 8192) g_bwd_cta[item][slot] = (val);                         \
   } while (0)
 #else
 #define BWD_TRACE(cond, ev, it) \
   do {                          \
+  } while (0)
+#define BWD_ITEM(item, slot, val) \
+  do {                            \
   } while (0)
 #endif
 
@@ -111,56 +140,108 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return FMT == 1 ? pack_bf16(a, b) : pack_f16(a, b);
 }
 
+// One work item = the 128 keys of key tile j of one (batch, head) slice.
+// Items are numbered slice-group-major: (batch, head) slices in groups of
+// BH_GROUP; inside a group, key tile 0 (the longest causal sweep) of every
+// slice first, then key tile 1, ... CTAs take items in that order from a
+// global counter, so the slices in flight at once stay few enough for their
+// Q, K, V, dO and fp32 dQ rows to share L2, every SM stays busy to the end,
+// and the last items are short.
+struct Item {
+  int bh, b, h, kv0, i0, n;
+};
+__device__ __forceinline__ Item decode_item(int item, const Params& p) {
+  const int nkt = (p.N + BN - 1) / BN;
+  const int g = item / (BH_GROUP * nkt);
+  const int rem = item - g * BH_GROUP * nkt;
+  const int gsz = min(BH_GROUP, p.BH - g * BH_GROUP);
+  const int j = rem / gsz;
+  Item it;
+  it.bh = g * BH_GROUP + rem % gsz;
+  it.b = it.bh / p.H;
+  it.h = it.bh % p.H;
+  it.kv0 = j * BN;
+  it.i0 = p.causal ? (it.kv0 / BM) : 0;
+  it.n = (p.N + BM - 1) / BM - it.i0;  // >= 1 since kv0 < N
+  return it;
+}
+
+// Persistent: one CTA per SM. Its producer warp takes the next work item
+// from p.work_counter and passes the id to the other roles through a small
+// ring (item_full / item_empty); id >= n_items ends every role's loop. Every
+// per-tile barrier completes once per query tile, so its phase is the
+// CTA-wide running tile count g (across items), and kv_full / kv_empty
+// complete once per item.
 template <int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
               const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
               const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  // No static shared memory is declared, so the dynamic block starts at the
+  // (1 KiB-aligned) base of the CTA's window; the 128-byte swizzle needs
+  // 1 KiB-aligned tiles and there is no room left for realignment padding.
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicCAS(&g_lsb_device_error, 0, 0xB00);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;                 // [NQS]
+  uint64_t* kv_empty = kv_full + 1;            // the item's last MMA has read K and V
+  uint64_t* q_full = kv_empty + 1;             // [NQS]
   uint64_t* q_empty = q_full + NQS;            // [NQS]
-  uint64_t* s_ready = q_empty + NQS;           // [2]: per S^T buffer
-  uint64_t* dp_ready = s_ready + 2;
-  uint64_t* p_ready = dp_ready + 1;            // [2]: per S^T buffer
-  uint64_t* ds_ready = p_ready + 2;
-  uint64_t* dv_done = ds_ready + 1;
-  uint64_t* dk_done = dv_done + 1;
-  uint64_t* dq_ready = dk_done + 1;
+  uint64_t* stat_full = q_empty + NQS;         // [NQS]: log-sum-exp / Dsum staged
+  uint64_t* do_full = stat_full + NQS;
+  uint64_t* do_empty = do_full + 1;            // dV (the last reader of dO) has completed
+  uint64_t* s_ready = do_empty + 1;
+  uint64_t* p_ready = s_ready + 1;
+  uint64_t* dp_ready = p_ready + 1;
+  uint64_t* ds_ready = dp_ready + 1;
+  uint64_t* dq_ready = ds_ready + 1;
   uint64_t* dq_free = dq_ready + 1;
-  uint64_t* stat_full = dq_free + 1;           // [NQS]: log-sum-exp / Dsum staged
-  uint64_t* red_full = stat_full + NQS;        // dQ tile staged (256 arrivals)
-  uint64_t* red_free = red_full + 1;           // its bulk reduction has read it
-  float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [NQS][lse2 64 | dsum 64]
+  uint64_t* dk_done = dq_free + 1;
+  // dQ staging, once per tile each: [0] warpgroup 1's 64 query rows (own
+  // buffer), [1] warpgroup 2's (in the dS^T tile). red_full: staged (128
+  // arrivals); red_free: the bulk reduction has read it.
+  uint64_t* red_full = dk_done + 1;            // [2]
+  uint64_t* red_free = red_full + 2;           // [2]
+  float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [NQS][lse2 BM | dsum BM]
+  uint64_t* item_full = red_free + 2;          // [NIS]
+  uint64_t* item_empty = item_full + NIS;      // [NIS]: 10 arrivals (MMA, reducer, 8 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SLOT_OFF);
+  volatile int* item_ids = reinterpret_cast<volatile int*>(smem + ITEM_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x;  // key tile (ascending = most query tiles first when causal)
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh % p.H;
-  const int kv0 = j * BN;
-  const int nq_all = (p.N + BM - 1) / BM;
-  const int i0 = p.causal ? (kv0 / BM) : 0;
-  const int n = nq_all - i0;  // >= 1 since kv0 < N
+  const int n_items = p.BH * ((p.N + BN - 1) / BN);
+  // Consumer side of the work-item ring: id of the k-th item (>= n_items:
+  // no more work), or -1 when the wait gave up.
+  auto next_item = [&](int k, bool arrive) -> int {
+    const int slot = k % NIS;
+    if (!mbar_wait(&item_full[slot], (k / NIS) & 1, 0x50A)) return -1;
+    const int id = item_ids[slot];
+    if (arrive) mbar_arrive(&item_empty[slot]);
+    return id;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
     for (int s = 0; s < NQS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
       mbar_init(&stat_full[s], 32);
     }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s_ready[i], 1); mbar_init(&p_ready[i], 256); }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
+    mbar_init(s_ready, 1);
+    mbar_init(p_ready, 256);
     mbar_init(dp_ready, 1);
     mbar_init(ds_ready, 256);
-    mbar_init(dv_done, 1);
-    mbar_init(dk_done, 1);
     mbar_init(dq_ready, 1);
     mbar_init(dq_free, 256);
-    mbar_init(red_full, 256);
-    mbar_init(red_free, 1);
+    mbar_init(dk_done, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&red_full[i], 128); mbar_init(&red_free[i], 1); }
+    for (int i = 0; i < NIS; ++i) { mbar_init(&item_full[i], 1); mbar_init(&item_empty[i], 10); }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -177,278 +258,334 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint8_t* sQ = smem + Q_OFF;
   uint8_t* sDO = smem + DO_OFF;
   uint8_t* sDS = smem + DS_OFF;
+  uint8_t* sSTG = smem + STG_OFF;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
-    reg_dealloc<72>();
-    const float* lse_bh = p.lse + (int64_t)bh * p.N;
-    const float* dsum_bh = p.dsum + (int64_t)bh * p.N;
+    reg_dealloc<112>();
     if (lane == 0) {
       prefetch_tmap(&tq); prefetch_tmap(&tk); prefetch_tmap(&tv); prefetch_tmap(&tdo);
-      mbar_arrive_expect_tx(kv_full, 2 * KC * KV_CHUNK);
-      for (int kc = 0; kc < KC; ++kc) {
-        tma_load_4d(sK + kc * KV_CHUNK, &tk, kv_full, kc * 64, kv0, h, b);
-        tma_load_4d(sV + kc * KV_CHUNK, &tv, kv_full, kc * 64, kv0, h, b);
-      }
     }
-    for (int it = 0; it < n; ++it) {
-      const int s = it % NQS;
-      // Stage s is reused once the MMAs of tile it-NQS (and so every read of
-      // its statistics, which precede ds_ready) have completed.
-      if (it >= NQS && !mbar_wait_warp(&q_empty[s], ((it / NQS) - 1) & 1, 0x501)) break;
-      const int m0 = (i0 + it) * BM;
+    int g = 0;  // running query-tile count of this CTA
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int slot = k % NIS;
+      if (k >= NIS && !mbar_wait_warp(&item_empty[slot], ((k / NIS) - 1) & 1, 0x504)) break;
+      int item = 0;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&q_full[s], 2 * KC * Q_CHUNK);
-        for (int kc = 0; kc < KC; ++kc) {
-          tma_load_4d(sQ + (s * KC + kc) * Q_CHUNK, &tq, &q_full[s], kc * 64, m0, h, b);
-          tma_load_4d(sDO + (s * KC + kc) * Q_CHUNK, &tdo, &q_full[s], kc * 64, m0, h, b);
+        item = atomicAdd(p.work_counter, 1);
+        item_ids[slot] = item;
+        mbar_arrive(&item_full[slot]);  // release: the id is visible to its waiters
+      }
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= n_items) break;
+      const Item w = decode_item(item, p);
+      BWD_ITEM(item, 0, gtimer());
+      const float* lse_bh = p.lse + (int64_t)w.bh * p.N;
+      const float* dsum_bh = p.dsum + (int64_t)w.bh * p.N;
+      for (int it = 0; it < w.n; ++it, ++g) {
+        const int s = g % NQS;
+        // Stage s is reused once the MMAs of tile g-NQS (and so every read of
+        // its statistics, which precede ds_ready) have completed.
+        if (g >= NQS && !mbar_wait_warp(&q_empty[s], ((g / NQS) - 1) & 1, 0x501)) { ok = false; break; }
+        const int m0 = (w.i0 + it) * BM;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[s], TILE);
+          for (int kc = 0; kc < KC; ++kc)
+            tma_load_4d(sQ + s * TILE + kc * CHUNK, &tq, &q_full[s], kc * 64, m0, w.h, w.b);
+        }
+        // Per-query statistics of this tile: log2-scaled LSE and Dsum.
+        float* st = stats + s * 2 * BM;
+#pragma unroll
+        for (int u = 0; u < BM / 32; ++u) {
+          const int c = lane + 32 * u;
+          const bool in = m0 + c < p.N;
+          st[c] = in ? __ldg(lse_bh + m0 + c) * 1.4426950408889634f : 0.f;
+          st[BM + c] = in ? __ldg(dsum_bh + m0 + c) : 0.f;
+        }
+        mbar_arrive(&stat_full[s]);
+        // dO(g) replaces dO(g-1) once dV(g-1) has read it.
+        if (g > 0 && !mbar_wait_warp(do_empty, (g - 1) & 1, 0x502)) { ok = false; break; }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(do_full, TILE);
+          for (int kc = 0; kc < KC; ++kc)
+            tma_load_4d(sDO + kc * CHUNK, &tdo, do_full, kc * 64, m0, w.h, w.b);
+        }
+        // K / V of this item replace the previous item's once all its MMAs
+        // are done (after this item's first Q and dO are on their way).
+        if (it == 0) {
+          if (k > 0 && !mbar_wait_warp(kv_empty, (k - 1) & 1, 0x503)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(kv_full, 2 * TILE);
+            for (int kc = 0; kc < KC; ++kc) {
+              tma_load_4d(sK + kc * CHUNK, &tk, kv_full, kc * 64, w.kv0, w.h, w.b);
+              tma_load_4d(sV + kc * CHUNK, &tv, kv_full, kc * 64, w.kv0, w.h, w.b);
+            }
+          }
         }
       }
-      // Per-query statistics of this tile: log2-scaled LSE and Dsum.
-      float* st = stats + s * 2 * BM;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = lane + 32 * u;
-        const bool in = m0 + c < p.N;
-        st[c] = in ? __ldg(lse_bh + m0 + c) * 1.4426950408889634f : 0.f;
-        st[BM + c] = in ? __ldg(dsum_bh + m0 + c) : 0.f;
-      }
-      mbar_arrive(&stat_full[s]);
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
-    reg_dealloc<72>();
+    reg_dealloc<112>();
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, BM, FMT, 0, 0);   // K-major A and B
-      constexpr uint32_t ID_DV = idesc_f16(128, D, FMT, 0, 1);   // B (dO, Q) MN-major
+      constexpr uint32_t ID_ACC = idesc_f16(128, D, FMT, 0, 1);  // TS; B (dO, Q) MN-major
       constexpr uint32_t ID_DQ = idesc_f16(128, BM, FMT, 1, 1);  // A (K^T), B (dS^T) MN-major
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO), ds_base = smem_u32(sDS);
-      // X^T = A B^T with A the [128][D] K or V tile, B the [64][D] Q or dO tile.
+      // X^T = A B^T with A the [128][D] K or V tile, B the [BM][D] Q or dO tile.
       auto issue_t = [&](uint32_t d_col, uint32_t a_base, uint32_t b_base) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = smem_desc_sw128(a_base + (kk / 4) * KV_CHUNK + (kk % 4) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(b_base + (kk / 4) * Q_CHUNK + (kk % 4) * 32, 16, 1024);
+          const uint64_t a = smem_desc_sw128(a_base + (kk / 4) * CHUNK + (kk % 4) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(b_base + (kk / 4) * CHUNK + (kk % 4) * 32, 16, 1024);
           mma_ss(tmem + d_col, a, bd, ID_S, kk > 0);
         }
       };
-      // Acc[128 keys][D] += A_tmem[128][64 q] * B[64 q][D]  (B MN-major, rows = q)
-      auto issue_acc = [&](uint32_t d_col, uint32_t a_col, uint32_t b_base, bool acc) {
+      // Acc[128 keys][D] += A_tmem[128][BM q] * B[BM q][D]  (B MN-major, rows = q).
+      // Warpgroup g packed the 16-bit values of its query columns [64g, 64g+64)
+      // into TMEM columns T_S + 64g + a_off + [0, 32): K-step kk (queries
+      // [16kk, 16kk+16)) reads 8 columns there.
+      auto issue_acc = [&](uint32_t d_col, uint32_t a_off, uint32_t b_base, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk) {
-          const uint64_t bd = smem_desc_sw128(b_base + kk * 2048, Q_CHUNK, 1024);
-          // Each warpgroup packs its 32 query columns into the first 16 TMEM
-          // columns of its own 32-column fp32 half, so the other warpgroup's
-          // unread scores are never overwritten: K-steps 0-1 read [0,16),
-          // K-steps 2-3 read [32,48) of the buffer.
-          mma_ts(tmem + d_col, tmem + a_col + (kk >> 1) * 32 + (kk & 1) * 8, bd, ID_DV,
+          const uint64_t bd = smem_desc_sw128(b_base + kk * 2048, CHUNK, 1024);
+          mma_ts(tmem + d_col, tmem + T_S + (kk >> 2) * 64 + a_off + (kk & 3) * 8, bd, ID_ACC,
                  (acc || kk > 0) ? 1u : 0u);
         }
       };
-      // S^T is double-buffered in TMEM, so S^T(it+2) is issued as soon as
-      // dV(it) has read P^T(it) from the same buffer; the conversion
-      // warpgroups never wait for the MMA chain of the previous tile.
-      auto issue_s = [&](int jt) {
-        issue_t(T_S + (jt & 1) * 64, k_base, q_base + (jt % NQS) * KC * Q_CHUNK);
-        mma_commit(&s_ready[jt & 1]);
-        BWD_TRACE(true, 1, jt);
-      };
-      bool ok = mbar_wait(kv_full, 0, 0x601) && mbar_wait(&q_full[0], 0, 0x602);
-      if (ok) {
+      // S^T(g) and dP^T(g). dP^T overwrites dQ^T(g-1) once the warpgroups
+      // have loaded it (dq_free).
+      auto issue_s_dp = [&](int gg) -> bool {
+        const int s = gg % NQS;
+        if (!mbar_wait(&q_full[s], (gg / NQS) & 1, 0x605)) return false;
         tc_fence_after();
-        issue_s(0);
+        issue_t(T_S, k_base, q_base + s * TILE);
+        mma_commit(s_ready);
+        BWD_TRACE(true, 1, gg);
+        if ((gg > 0 && !mbar_wait(dq_free, (gg - 1) & 1, 0x606)) ||
+            !mbar_wait(do_full, gg & 1, 0x608))
+          return false;
+        tc_fence_after();
         issue_t(T_DP, v_base, do_base);
         mma_commit(dp_ready);
-        if (n > 1) {
-          ok = mbar_wait(&q_full[1], 0, 0x609);
+        BWD_TRACE(true, 6, gg);
+        return true;
+      };
+      int g = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int item = next_item(k, true);
+        if (item < 0 || item >= n_items) break;
+        const Item w = decode_item(item, p);
+        if (!mbar_wait(kv_full, k & 1, 0x601)) { ok = false; break; }
+        tc_fence_after();
+        if (!issue_s_dp(g)) { ok = false; break; }
+        for (int it = 0; it < w.n; ++it, ++g) {
+          const int s = g % NQS;
+          const uint32_t ph = g & 1;
+          // dV(0) of an item overwrites the previous item's dV: the
+          // warpgroups read it out (epilogue) before their p_ready.
+          if (!mbar_wait(p_ready, ph, 0x603)) { ok = false; break; }
+          BWD_TRACE(true, 2, g);
           tc_fence_after();
-          if (ok) issue_s(1);
-        }
-      }
-      for (int it = 0; ok && it < n; ++it) {
-        const int s = it % NQS;
-        const uint32_t ph = it & 1;
-        if (!mbar_wait(&p_ready[it & 1], (it >> 1) & 1, 0x603)) { ok = false; break; }
-        BWD_TRACE(true, 2, it);
-        tc_fence_after();
-        issue_acc(T_DV, T_S + (it & 1) * 64, do_base + s * KC * Q_CHUNK, it > 0);
-        mma_commit(dv_done);
-        BWD_TRACE(true, 3, it);
-        if (!mbar_wait(ds_ready, ph, 0x606)) { ok = false; break; }
-        BWD_TRACE(true, 4, it);
-        tc_fence_after();
-        if (it + 1 < n) {
-          // dS^T(it) lives in S buffer it & 1, so dP^T(it+1) may overwrite
-          // dP^T(it) as soon as both warpgroups have read it (ds_ready).
-          issue_t(T_DP, v_base, do_base + ((it + 1) % NQS) * KC * Q_CHUNK);
-          mma_commit(dp_ready);
-        }
-        issue_acc(T_DK, T_S + (it & 1) * 64 + 16, q_base + s * KC * Q_CHUNK, it > 0);
-        mma_commit(dk_done);
-        BWD_TRACE(true, 5, it);
-        if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, 0x607)) { ok = false; break; }
-        tc_fence_after();
+          issue_acc(T_DV, 0, do_base, it > 0);
+          mma_commit(do_empty);
+          if (!mbar_wait(ds_ready, ph, 0x604)) { ok = false; break; }
+          BWD_TRACE(true, 4, g);
+          tc_fence_after();
+          // dQ^T(g) = K^T dS^T over the 128 keys, into the dP^T columns
+          // (every read of dP^T(g) preceded ds_ready).
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = smem_desc_sw128(k_base + kk * 2048, KV_CHUNK, 1024);
-          const uint64_t bd = smem_desc_sw128(ds_base + (it & 1) * DS_BYTES + kk * 2048, DS_BYTES, 1024);
-          mma_ss(tmem + T_DQ, a, bd, ID_DQ, kk > 0);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t a = smem_desc_sw128(k_base + kk * 2048, CHUNK, 1024);
+            const uint64_t bd = smem_desc_sw128(ds_base + kk * 2048, CHUNK, 1024);
+            mma_ss(tmem + T_DP, a, bd, ID_DQ, kk > 0);
+          }
+          mma_commit(dq_ready);
+          issue_acc(T_DK, 32, q_base + s * TILE, it > 0);
+          mma_commit(dk_done);
+          mma_commit(&q_empty[s]);
+          BWD_TRACE(true, 5, g);
+          // tcgen05.mma instructions of one thread execute in issue order, so
+          // S^T(g+1) overwrites P^T / dS^T(g) only after dV(g) and dK(g)
+          // have read them.
+          if (it + 1 < w.n && !issue_s_dp(g + 1)) { ok = false; break; }
         }
-        mma_commit(dq_ready);
-        BWD_TRACE(true, 6, it);
-        mma_commit(&q_empty[s]);
-        if (it + 2 < n) {
-          // S^T(it+2) overwrites P^T(it) and dS^T(it) in buffer it & 1:
-          // dV(it) and dK(it) must have read them.
-          if (!mbar_wait(&q_full[(it + 2) % NQS], ((it + 2) / NQS) & 1, 0x604) ||
-              !mbar_wait(dk_done, ph, 0x605)) { ok = false; break; }
-          tc_fence_after();
-          issue_s(it + 2);
-        }
+        mma_commit(kv_empty);  // every MMA of this item (all reads of K, V) done
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------- dQ reducer --
-    // Adds each staged 64-row dQ tile into the fp32 dQ buffer (rows are
-    // contiguous there) with one bulk reduction. Tiles are staged one tile
-    // late, so the staging buffer is normally read by the time it is reused.
-    reg_dealloc<72>();
+    // Adds each staged 64-row dQ half-tile into the fp32 dQ buffer (rows are
+    // contiguous there) with one bulk reduction per half; the dS^T-tile half
+    // goes first, since the next dS^T write waits for it to be read.
+    reg_dealloc<112>();
     if (lane == 0) {
-      for (int it = 0; it < n; ++it) {
-        if (!mbar_wait(red_full, it & 1, 0x901)) break;
-        const int m0 = (i0 + it) * BM;
-        const int rows = min(BM, p.N - m0);
-        bulk_reduce_add_f32(p.dq_acc + ((int64_t)bh * p.N + m0) * D,
-                            reinterpret_cast<const float*>(smem + RED_OFF), rows * D * 4);
-        bulk_commit();
-        bulk_wait_read();  // the staging tile may be rewritten once this has read it
-        mbar_arrive(red_free);
+      int g = 0;
+      bool ok = true;
+      for (int kk = 0; ok; ++kk) {
+        const int item = next_item(kk, true);
+        if (item < 0 || item >= n_items) break;
+        const Item w = decode_item(item, p);
+        for (int it = 0; it < w.n; ++it, ++g) {
+          const uint32_t ph = g & 1;
+          const int64_t m0 = (int64_t)(w.i0 + it) * BM;
+          for (int k = 1; k >= 0 && ok; --k) {
+            ok = mbar_wait(&red_full[k], ph, 0x901);
+            const int rows = (int)min((int64_t)STAGE_ROWS, p.N - (m0 + k * STAGE_ROWS));
+#ifdef LSB_BWD_NORED
+            if (false)
+#else
+            if (ok && rows > 0)
+#endif
+              bulk_reduce_add_f32(p.dq_acc + ((int64_t)w.bh * p.N + m0 + k * STAGE_ROWS) * D,
+                                  reinterpret_cast<const float*>(k ? sDS : sSTG), rows * D * 4);
+            bulk_commit();  // an empty group when nothing was issued
+          }
+          if (!ok) break;
+          bulk_wait_read_1();
+          mbar_arrive(&red_free[1]);
+          bulk_wait_read();
+          mbar_arrive(&red_free[0]);
+        }
       }
       bulk_wait_all();  // every reduction has landed before the CTA exits
     }
   } else if (warp < 4) {
-    reg_dealloc<72>();
+    reg_dealloc<112>();
   } else {
     // ------------------------------------------------------------------------
-    // Two warpgroups split the 64 query columns of each tile (32 each):
+    // Two warpgroups split the 128 query columns of each tile (64 each):
     // thread = key (TMEM lane) for P^T / dS^T, then thread = head-dim index
-    // for its half of the dQ^T columns. Epilogue: warpgroup 1 writes dV,
-    // warpgroup 2 writes dK.
-    reg_alloc<216>();
-    const int half = warp >> 3;                  // 0: q cols [0,32), 1: [32,64)
+    // for its 64 dQ^T columns. Item epilogue: warpgroup 1 writes dV,
+    // warpgroup 2 dK, while the next item's K / V load and first S^T run.
+    reg_alloc<176>();
+    const int half = warp >> 3;                  // 0: q cols [0,64), 1: [64,128)
     const int r = (threadIdx.x & 127);           // TMEM lane: key, then head-dim index
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const int key = kv0 + r;
     const float sl2 = p.scale_log2;
-    const int cb = half * 32;                    // first query column of this half
-    // dQ^T columns [cb, cb+32) of tile jt: thread = head-dim index r. The 32
-    // query rows are staged [q][d] in shared memory; warp 2 adds the whole
-    // 64-row tile into the fp32 dQ buffer with one bulk reduction.
-    auto stage_dq = [&](int jt) -> bool {
-      if (!mbar_wait_warp(dq_ready, jt & 1, 0x801)) return false;
-      BWD_TRACE(r == 0 && half == 0, 11, jt);
-      tc_fence_after();
-      uint32_t qv[32];
-      tmem_ld32(lane_addr + T_DQ + cb, qv);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(dq_free);
-      if (jt >= 1 && !mbar_wait_warp(red_free, (jt - 1) & 1, 0x802)) return false;
-      float* stage = reinterpret_cast<float*>(smem + RED_OFF) + half * 32 * D;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) stage[c * D + r] = __uint_as_float(qv[c]) * p.scale;
-      fence_proxy_async_smem();
-      mbar_arrive(red_full);
-      BWD_TRACE(r == 0 && half == 0, 12, jt);
-      return true;
-    };
+    const int cb = half * 64;                    // first query column of this half
+    const uint32_t my_s = lane_addr + T_S + cb;  // this half's S^T columns
+    int g = 0;
     bool ok = true;
-    for (int it = 0; it < n; ++it) {
-      const uint32_t ph = it & 1;
-      const int m0 = (i0 + it) * BM;
-      const float* st = stats + (it % NQS) * 2 * BM;
-      const uint32_t sbuf = T_S + (it & 1) * 64;
-      if (!mbar_wait_warp(&stat_full[it % NQS], (it / NQS) & 1, 0x705)) { ok = false; break; }
-      if (!mbar_wait_warp(&s_ready[it & 1], (it >> 1) & 1, 0x701)) { ok = false; break; }
-      BWD_TRACE(r == 0 && half == 0, 7, it);
-      tc_fence_after();
-      uint32_t sv[32];
-      tmem_ld32(lane_addr + sbuf + cb, sv);
-      tmem_ld_wait();
-      // Masks: causal (q < key), and rows/columns past the sequence end.
-      const bool need_mask = (m0 + BM > p.N) || (kv0 + BN > p.N) || (p.causal && m0 < kv0 + BN);
+    for (int k = 0; ok; ++k) {
+      int item = 0;
+      if (lane == 0) item = next_item(k, true);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item < 0 || item >= n_items) break;
+      const Item w = decode_item(item, p);
+      const int key = w.kv0 + r;
       const int qlo = p.causal ? key : 0;  // first valid q for this key
-      float pf[32];
-      uint32_t pk[16];
+      for (int it = 0; it < w.n; ++it, ++g) {
+        const uint32_t ph = g & 1;
+        const int m0 = (w.i0 + it) * BM;
+        const float* st = stats + (g % NQS) * 2 * BM;
+        if (!mbar_wait_warp(&stat_full[g % NQS], (g / NQS) & 1, 0x705)) { ok = false; break; }
+        if (!mbar_wait_warp(s_ready, ph, 0x701)) { ok = false; break; }
+        BWD_TRACE(r == 0 && half == 0, 7, g);
+        if (it == 0 && r == 0 && half == 0) BWD_ITEM(item, 1, gtimer());
+        tc_fence_after();
+        uint32_t sv[64];
+        tmem_ld32(my_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(my_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        // Masks: causal (q < key), and rows/columns past the sequence end.
+        const bool need_mask =
+            (m0 + BM > p.N) || (w.kv0 + BN > p.N) || (p.causal && m0 < w.kv0 + BN);
+        float pf[64];
+        uint32_t pk[32];
+        // The mask test is hoisted out of the exp2 loop: a branch per element
+        // pair would cut the loop into blocks too small to hide MUFU latency.
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const int c0 = cb + 2 * cc;
-        const float2 l2 = *reinterpret_cast<const float2*>(st + c0);  // shared broadcast
-        float p0 = ex2(fmaf(__uint_as_float(sv[2 * cc]), sl2, -l2.x));
-        float p1 = ex2(fmaf(__uint_as_float(sv[2 * cc + 1]), sl2, -l2.y));
+        for (int cc = 0; cc < 32; ++cc) {
+          const float2 l2 = *reinterpret_cast<const float2*>(st + cb + 2 * cc);  // shared broadcast
+          pf[2 * cc] = ex2(fmaf(__uint_as_float(sv[2 * cc]), sl2, -l2.x));
+          pf[2 * cc + 1] = ex2(fmaf(__uint_as_float(sv[2 * cc + 1]), sl2, -l2.y));
+        }
         if (need_mask) {
-          const int q0 = m0 + c0;
-          if (key >= p.N || q0 >= p.N || q0 < qlo) p0 = 0.f;
-          if (key >= p.N || q0 + 1 >= p.N || q0 + 1 < qlo) p1 = 0.f;
-        }
-        pf[2 * cc] = p0;
-        pf[2 * cc + 1] = p1;
-        pk[cc] = pack2<FMT>(p0, p1);
-      }
-      tmem_st16(lane_addr + sbuf + half * 32, pk);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_ready[it & 1]);
-      BWD_TRACE(r == 0 && half == 0, 8, it);
-
-      if (!mbar_wait_warp(dp_ready, ph, 0x702)) { ok = false; break; }
-      BWD_TRACE(r == 0 && half == 0, 9, it);
-      tc_fence_after();
-      tmem_ld32(lane_addr + T_DP + cb, sv);
-      tmem_ld_wait();
-      uint32_t dsk[16];
+          const int qhi = min(p.N - (m0 + cb), 64);  // columns c < qhi are real queries
+          const int clo = key >= p.N ? 64 : qlo - (m0 + cb);  // columns c < clo are masked
 #pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        const float2 ds2 = *reinterpret_cast<const float2*>(st + BM + cb + 2 * cc);
-        dsk[cc] = pack2<FMT>(pf[2 * cc] * (__uint_as_float(sv[2 * cc]) - ds2.x),
-                             pf[2 * cc + 1] * (__uint_as_float(sv[2 * cc + 1]) - ds2.y));
-      }
-      tmem_st16(lane_addr + sbuf + half * 32 + 16, dsk);  // beside P^T, in the S buffer
-      // dS^T row half -> shared (128-byte swizzle) for the dQ^T GEMM, once the
-      // previous dQ^T GEMM has finished reading the buffer.
-      // dS^T buffer it & 1 was last read by dQ^T(it-2), which stage_dq(it-2)
-      // waited for during the previous tile.
-      {
-        uint8_t* rowp = sDS + (it & 1) * DS_BYTES + r * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int chunk = half * 4 + c;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dsk[4 * c], dsk[4 * c + 1], dsk[4 * c + 2], dsk[4 * c + 3]);
+          for (int c = 0; c < 64; ++c)
+            if (c < clo || c >= qhi) pf[c] = 0.f;
         }
-      }
-      fence_proxy_async_smem();
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(ds_ready);
-      BWD_TRACE(r == 0 && half == 0, 10, it);
-      // The previous tile's dQ^T (complete by now) is staged while dK(it) and
-      // dQ^T(it) run on the tensor cores.
-      if (it > 0 && !stage_dq(it - 1)) { ok = false; break; }
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) pk[cc] = pack2<FMT>(pf[2 * cc], pf[2 * cc + 1]);
+        // P^T into the first 32 columns of this half's own S^T range (the
+        // other warpgroup's unread scores are never overwritten).
+        tmem_st32(my_s, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_ready);
+        BWD_TRACE(r == 0 && half == 0, 8, g);
 
-    }
-    if (ok && !stage_dq(n - 1)) ok = false;
-    // Epilogue: warpgroup 1 writes this key's dV row, warpgroup 2 its dK row.
-    if (ok && mbar_wait_warp(dk_done, (n - 1) & 1, 0x704)) {
+        if (!mbar_wait_warp(dp_ready, ph, 0x702)) { ok = false; break; }
+        BWD_TRACE(r == 0 && half == 0, 9, g);
+        tc_fence_after();
+        tmem_ld32(lane_addr + T_DP + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(lane_addr + T_DP + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int cc = 0; cc < 32; ++cc) {
+          const float2 ds2 = *reinterpret_cast<const float2*>(st + BM + cb + 2 * cc);
+          pk[cc] = pack2<FMT>(pf[2 * cc] * (__uint_as_float(sv[2 * cc]) - ds2.x),
+                              pf[2 * cc + 1] * (__uint_as_float(sv[2 * cc + 1]) - ds2.y));
+        }
+        tmem_st32(my_s + 32, pk);  // dS^T beside P^T
+        // dS^T row -> shared chunk `half` (128-byte swizzle) for the dQ^T GEMM,
+        // once the bulk reduction has read the previous tile's second dQ
+        // staging half from the same buffer.
+        if (g > 0 && !mbar_wait_warp(&red_free[1], (g - 1) & 1, 0x703)) { ok = false; break; }
+        {
+          uint8_t* rowp = sDS + half * CHUNK + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(ds_ready);
+        BWD_TRACE(r == 0 && half == 0, 10, g);
+
+        // dQ^T(g), thread = head-dim index r, this half's 64 query columns.
+        if (!mbar_wait_warp(dq_ready, ph, 0x704)) { ok = false; break; }
+        BWD_TRACE(r == 0 && half == 0, 11, g);
+        tc_fence_after();
+        tmem_ld32(lane_addr + T_DP + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(lane_addr + T_DP + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_free);
+        // Warpgroup 1 reuses its buffer once the previous tile's rows have been
+        // read; warpgroup 2's half of the dS^T tile is free (dQ^T(g) is done).
+        if (half == 0 && g > 0 && !mbar_wait_warp(&red_free[0], (g - 1) & 1, 0x706)) {
+          ok = false;
+          break;
+        }
+        float* stage = reinterpret_cast<float*>(half == 0 ? sSTG : sDS);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) stage[c * D + r] = __uint_as_float(sv[c]) * p.scale;
+        fence_proxy_async_smem();
+        mbar_arrive(&red_full[half]);
+        BWD_TRACE(r == 0 && half == 0, 12, g);
+      }
+      if (!ok) break;
+      // Item epilogue: warpgroup 1 writes this key's dV row, warpgroup 2 its
+      // dK row. The next item's dV(0) / dK(0) overwrite these columns only
+      // after this warpgroup's p_ready of that tile.
+      if (!mbar_wait_warp(dk_done, (g - 1) & 1, 0x707)) { ok = false; break; }
       tc_fence_after();
       // tcgen05.ld is warp-collective: every lane loads, only valid keys store.
       const bool store = key < p.N;
       const uint32_t col = half == 0 ? T_DV : T_DK;
       const float mul = half == 0 ? 1.f : p.scale;
       uint8_t* dst = half == 0
-          ? reinterpret_cast<uint8_t*>(p.dv) + 2 * (b * p.sdv_b + h * p.sdv_h + (int64_t)key * p.sdv_n)
-          : reinterpret_cast<uint8_t*>(p.dk) + 2 * (b * p.sdk_b + h * p.sdk_h + (int64_t)key * p.sdk_n);
+          ? reinterpret_cast<uint8_t*>(p.dv) + 2 * (w.b * p.sdv_b + w.h * p.sdv_h + (int64_t)key * p.sdv_n)
+          : reinterpret_cast<uint8_t*>(p.dk) + 2 * (w.b * p.sdk_b + w.h * p.sdk_h + (int64_t)key * p.sdk_n);
 #pragma unroll
       for (int i = 0; i < D / 32; ++i) {
         uint32_t v[32];
@@ -465,6 +602,16 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             d4[v4] = make_uint4(pk2[4 * v4], pk2[4 * v4 + 1], pk2[4 * v4 + 2], pk2[4 * v4 + 3]);
         }
       }
+      tc_fence_before();
+      if (r == 0 && half == 0) BWD_ITEM(item, 2, gtimer());
+#ifdef LSB_BWD_TRACE
+      if (r == 0 && half == 0) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        BWD_ITEM(item, 3, smid);
+        BWD_ITEM(item, 4, w.n);
+      }
+#endif
     }
   }
 
@@ -478,6 +625,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 
 }  // namespace fa_bwd
 
+
 bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const void* o,
                           const void* dout, const void* dq, const void* dk, const void* dv,
                           int64_t B, int64_t H, int64_t N, int64_t D, const int64_t* sq,
@@ -487,7 +635,7 @@ bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const voi
   (void)o; (void)so; (void)dq; (void)sdq;
   if (dtype != LSB_DTYPE_BF16 && dtype != LSB_DTYPE_F16) return false;
   if (D != fa_bwd::D) return false;
-  if (B * H > 65535 || N >= (1LL << 30)) return false;
+  if (N >= (1LL << 30) || B * H * ((N + fa_bwd::BN - 1) / fa_bwd::BN) > 0x7fffffff) return false;
   if (!tma_ok(q, B, H, N, sq, 2) || !tma_ok(k, B, H, N, sk, 2) || !tma_ok(v, B, H, N, sv, 2) ||
       !tma_ok(dout, B, H, N, sdo, 2))
     return false;
@@ -506,7 +654,7 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
                          const int64_t* sq, const int64_t* sk, const int64_t* sv,
                          const int64_t* sdo, const int64_t* sdk, const int64_t* sdv, float scale,
                          int causal, int dtype, const float* dsum, float* dq_acc,
-                         cudaStream_t st) {
+                         int* work_counter, cudaStream_t st) {
   using namespace fa_bwd;
   CUtensorMap mq, mk, mv, mdo;
   int rc = make_bhnd_map(&mq, q, dtype, B, H, N, D, sq, 64, BM);
@@ -516,16 +664,19 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
   if (rc) return rc;
   Params p;
   p.lse = lse; p.dsum = dsum; p.dq_acc = dq_acc; p.dk = dk; p.dv = dv;
+  p.work_counter = work_counter;
   p.sdk_b = sdk[0]; p.sdk_h = sdk[1]; p.sdk_n = sdk[2];
   p.sdv_b = sdv[0]; p.sdv_h = sdv[1]; p.sdv_n = sdv[2];
-  p.H = (int)H; p.N = (int)N;
+  p.H = (int)H; p.N = (int)N; p.BH = (int)(B * H);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   auto kern = fa_bwd_kernel<FMT>;
   LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
               "attn_bwd_tc smem attribute");
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)(B * H));
+  // Persistent: one CTA per SM (shared memory and TMEM allow no more).
+  const int64_t n_items = B * H * ((N + BN - 1) / BN);
+  dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));
   kern<<<grid, THREADS, SMEM, st>>>(mq, mk, mv, mdo, p);
   LSB_CHECK_LAUNCH("attn_bwd_tc");
   return LSB_OK;
@@ -542,12 +693,15 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   int rc = bf ? launch_dsum<__nv_bfloat16>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st)
               : launch_dsum<__half>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st);
   if (rc) return rc;
-  LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)(B * H * N * D), st),
+  // The work-item counter sits in the 256 bytes after the (256-byte padded)
+  // dQ accumulator (lsb_attn_bwd_workspace_size); one memset zeroes both.
+  int* work_counter = reinterpret_cast<int*>(reinterpret_cast<char*>(dq_acc) + align256(4 * B * H * N * D));
+  LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, (size_t)align256(4 * B * H * N * D) + sizeof(int), st),
               "attn_bwd dQ accumulator memset");
   rc = bf ? launch_fa_bwd<1>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,
-                             causal, dtype, dsum, dq_acc, st)
+                             causal, dtype, dsum, dq_acc, work_counter, st)
           : launch_fa_bwd<0>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,
-                             causal, dtype, dsum, dq_acc, st);
+                             causal, dtype, dsum, dq_acc, work_counter, st);
   if (rc) return rc;
   return bf ? launch_dq_cast<__nv_bfloat16>(dq_acc, dq, B, H, N, D, S4(sdq), st)
             : launch_dq_cast<__half>(dq_acc, dq, B, H, N, D, S4(sdq), st);
@@ -556,6 +710,9 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
 #ifdef LSB_BWD_TRACE
 extern "C" LSB_API int lsb_bwd_trace_read(long long* out) {
   return (int)cudaMemcpyFromSymbol(out, fa_bwd::g_bwd_trace, sizeof(fa_bwd::g_bwd_trace));
+}
+extern "C" LSB_API int lsb_bwd_item_read(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, fa_bwd::g_bwd_cta, sizeof(fa_bwd::g_bwd_cta));
 }
 #endif
 

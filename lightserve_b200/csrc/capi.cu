@@ -51,7 +51,6 @@ int attn_fwd_tc_device_error();
 int attn_bwd_tc_device_error();
 int paged_decode_device_error();
 
-static inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 }  // namespace lsb
 
@@ -97,7 +96,8 @@ extern "C" int lsb_attn_fwd(const void* q, const void* k, const void* v, void* o
 
 extern "C" int64_t lsb_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D) {
   if (B <= 0 || H <= 0 || N <= 0 || D <= 0) return 0;
-  return lsb::align256(4 * B * H * N) + lsb::align256(4 * B * H * N * D);
+  // Dsum, dQ accumulator, and the tcgen05 kernel's work-item counter.
+  return lsb::align256(4 * B * H * N) + lsb::align256(4 * B * H * N * D) + 256;
 }
 
 extern "C" int lsb_attn_bwd(const void* q, const void* k, const void* v, const void* o,

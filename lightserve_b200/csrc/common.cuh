@@ -141,4 +141,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Workspace regions are padded to 256 bytes.
+inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
 }  // namespace lsb

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_workspace_sizes():
     lib = _lib.load()
-    assert lib.lsb_attn_bwd_workspace_size(4, 32, 2048, 128) == 4 * 4 * 32 * 2048 + 4 * 4 * 32 * 2048 * 128
+    assert lib.lsb_attn_bwd_workspace_size(4, 32, 2048, 128) == 4 * 4 * 32 * 2048 + 4 * 4 * 32 * 2048 * 128 + 256
     assert lib.lsb_attn_bwd_workspace_size(0, 1, 1, 1) == 0
     # A context that fits one 512-token partition needs no scratch.
     assert lib.lsb_paged_decode_workspace_size(64, 16, 128, 32, 16) == 0

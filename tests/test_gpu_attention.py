@@ -98,7 +98,8 @@ def test_gradcheck(B, H, N, D, causal):
                                     eps=1e-3, atol=1e-2, rtol=1e-2)
 
 
-BWD_SHAPES = [(1, 1, 17, 32), (2, 2, 64, 64), (1, 4, 130, 64), (2, 8, 256, 128), (1, 2, 300, 128)]
+BWD_SHAPES = [(1, 1, 17, 32), (2, 2, 64, 64), (1, 4, 130, 64), (2, 8, 256, 128), (1, 2, 300, 128),
+              (1, 2, 1000, 128)]
 
 
 @pytest.mark.parametrize("causal", [False, True])
