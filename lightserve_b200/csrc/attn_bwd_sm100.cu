@@ -104,6 +104,13 @@ struct Params {
   int causal;
 };
 
+// 32-byte global store (sm_100 256-bit vector store); dst 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -586,6 +593,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       uint8_t* dst = half == 0
           ? reinterpret_cast<uint8_t*>(p.dv) + 2 * (w.b * p.sdv_b + w.h * p.sdv_h + (int64_t)key * p.sdv_n)
           : reinterpret_cast<uint8_t*>(p.dk) + 2 * (w.b * p.sdk_b + w.h * p.sdk_h + (int64_t)key * p.sdk_n);
+      const bool st32 = (reinterpret_cast<uintptr_t>(dst) & 31) == 0;
 #pragma unroll
       for (int i = 0; i < D / 32; ++i) {
         uint32_t v[32];
@@ -595,7 +603,12 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 #pragma unroll
         for (int cc = 0; cc < 16; ++cc)
           pk2[cc] = pack2<FMT>(__uint_as_float(v[2 * cc]) * mul, __uint_as_float(v[2 * cc + 1]) * mul);
-        if (store) {
+        if (store && st32) {
+          // Whole 32-byte sectors per store: with one key row per thread,
+          // 16-byte stores reach about half the SM's write bandwidth.
+#pragma unroll
+          for (int v8 = 0; v8 < 2; ++v8) st_global_v8(dst + 64 * i + 32 * v8, &pk2[8 * v8]);
+        } else if (store) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + 64 * i);
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4)
