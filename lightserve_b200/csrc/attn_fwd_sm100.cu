@@ -6,25 +6,38 @@
 // causal and sequence-end masks, online softmax with fp32 row statistics,
 // P rounded to the input dtype before P V, O = acc / l, L = m + ln(l).
 //
-// B200 design (one CTA per 256 query rows of one (batch, head)):
-//  * warp 0: TMA producer. Q tiles once, then K and V tiles of 128 keys into a
-//    2-stage ring (128-byte-swizzled boxes of 64 head-dim columns).
-//  * warp 1: TMEM owner and single-thread MMA issuer. Two query tiles of 128
-//    rows share each K/V tile: S_t = Q_t K^T (SS MMA, fp32 in TMEM) and
-//    O_t += P_t V (TS MMA: P read from TMEM, V from shared memory).
+// B200 design: a persistent kernel, one CTA per SM. A work item is 256 query
+// rows (two tiles of 128) of one (batch, head); CTAs take items from a
+// global counter in slice-group order (groups of BH_GROUP (batch, head)
+// slices; inside a group the longest causal items first), so the slices in
+// flight share K / V in L2 and every SM stays busy to the end.
+//  * warp 0: TMA producer and work fetcher. Q tiles per item (each tile as
+//    soon as the previous item's last QK on it is done), K and V tiles of
+//    128 keys through a 2-stage ring that runs on across items.
+//  * warp 1: TMEM owner and single-thread MMA issuer. Two query tiles share
+//    each K/V tile: S_t = Q_t K^T (SS MMA, fp32 in TMEM) and O_t += P_t V
+//    (TS MMA: P read from TMEM, V from shared memory).
 //  * warpgroups 1 and 2: softmax for query tile 0 and 1, one thread per row
 //    (TMEM lane). Each thread loads its 128 scores with tcgen05.ld, takes the
 //    row max, exponentiates with ex2 on log2(e)-prescaled scores, writes P as
 //    packed 16-bit pairs over the first 64 columns of its S buffer, and
 //    rescales O in TMEM only when the running max grew by more than 2^8
 //    (otherwise the stale max is kept; values stay within fp32/bf16 range).
+//    At the end of an item the warpgroup normalises and stores its O rows
+//    and LSE, then starts the next item; that item's first PV overwrites O
+//    only after this warpgroup's p_full, so the read-out needs no barrier.
 //  * TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512) columns.
 //  * MMA order per K/V tile j: PV_0(j), QK_0(j+1), PV_1(j), QK_1(j+1), so each
-//    softmax warpgroup's work overlaps the other tile's two GEMMs.
-//  * Causal: query tile t of CTA c stops at its diagonal K/V tile; CTAs are
-//    issued heaviest first.
+//    softmax warpgroup's work overlaps the other tile's two GEMMs;
+//    tcgen05.mma instructions of one thread execute in issue order, so
+//    QK_t(j+1) may overwrite S_t right after PV_t(j) without a wait.
+//  * Every per-(tile, K/V step) barrier completes once per step, so its phase
+//    is that tile's running step count across items.
 //  * Every mbarrier wait is bounded (sm100.cuh); on a timeout the kernel
 //    records an error code, skips the rest of its work, frees TMEM and exits.
+#include <algorithm>
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -35,11 +48,16 @@ namespace fa_fwd {
 
 constexpr int BM = 128;      // query rows per tile (= TMEM lanes)
 constexpr int BN = 128;      // keys per K/V tile
-constexpr int TILES = 2;     // query tiles per CTA
+constexpr int TILES = 2;     // query tiles per work item
 constexpr int NS = 2;        // K/V ring stages
+constexpr int NIS = 4;       // work-item id ring slots
 constexpr int THREADS = 384;
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows][64 cols] 16-bit box
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+#ifndef LSB_FWD_GROUP
+#define LSB_FWD_GROUP 16
+#endif
+constexpr int BH_GROUP = LSB_FWD_GROUP;  // (batch, head) slices scheduled together
 
 template <int D>
 struct Smem {
@@ -48,22 +66,30 @@ struct Smem {
   static constexpr int K_OFF = Q_OFF + TILES * KC * CHUNK_BYTES;
   static constexpr int V_OFF = K_OFF + NS * KC * CHUNK_BYTES;
   static constexpr int BAR_OFF = V_OFF + NS * KC * CHUNK_BYTES;
-  // barriers: q_full, k_full[NS], v_full[NS], kv_empty[NS], s_full[2], p_full[2], pv_done[2]
-  static constexpr int NBAR = 1 + 3 * NS + 3 * TILES;
+  // barriers: q_full[2], q_empty[2], k_full[NS], v_full[NS], kv_empty[NS], s_full[2],
+  // p_full[2], pv_done[2], item_full[NIS], item_empty[NIS]
+  static constexpr int NBAR = 2 * TILES + 3 * NS + 3 * TILES + 2 * NIS;
   static constexpr int TMEM_SLOT_OFF = BAR_OFF + NBAR * 8;
-  static constexpr int BYTES = TMEM_SLOT_OFF + 16;
+  static constexpr int ITEM_OFF = TMEM_SLOT_OFF + 16;
+  static constexpr int BYTES = ITEM_OFF + NIS * 4;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
 };
 
 struct Params {
   void* o;
   float* lse;
+  int* work_counter;  // zeroed before launch; CTAs take work items from it
   int64_t so_b, so_h, so_n;
-  int H, N;
+  int H, N, BH;
   int num_q_ctas;
   float scale_log2;
   int causal;
 };
+
+// Work-item counters, one per in-flight launch (slot chosen per launch and
+// zeroed on the launch stream just before it).
+constexpr int COUNTER_SLOTS = 256;
+__device__ int g_work_counters[COUNTER_SLOTS];
 
 using namespace sm100;
 
@@ -71,6 +97,13 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// 32-byte global store (sm_100 256-bit vector store); dst 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
 }
 
 // Row max over a thread's 128 scores (three-input max, 8 independent partial
@@ -98,6 +131,34 @@ __device__ __forceinline__ float row_max(uint32_t (&sr)[4][32], int lim) {
                max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
 }
 
+// One work item: query rows [q0, q0 + 256) of one (batch, head) slice.
+struct Item {
+  int bh, b, h, q0;
+  int nkv_t[TILES];  // K/V tiles each query tile visits (0: tile past the end)
+  int nkv;
+};
+__device__ __forceinline__ Item decode_item(int item, const Params& p) {
+  const int nq = p.num_q_ctas;
+  const int g = item / (BH_GROUP * nq);
+  const int rem = item - g * BH_GROUP * nq;
+  const int gsz = min(BH_GROUP, p.BH - g * BH_GROUP);
+  const int ci = rem / gsz;
+  Item w;
+  w.bh = g * BH_GROUP + rem % gsz;
+  w.b = w.bh / p.H;
+  w.h = w.bh % p.H;
+  const int c = p.causal ? (nq - 1 - ci) : ci;  // causal: longest items first
+  w.q0 = c * (TILES * BM);
+  const int nkv_all = (p.N + BN - 1) / BN;
+#pragma unroll
+  for (int t = 0; t < TILES; ++t) {
+    const int qt0 = w.q0 + t * BM;
+    w.nkv_t[t] = qt0 >= p.N ? 0 : (p.causal ? min(nkv_all, qt0 / BN + 1) : nkv_all);
+  }
+  w.nkv = max(w.nkv_t[0], w.nkv_t[1]);
+  return w;
+}
+
 template <int D, int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -107,40 +168,47 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 1 + NS;
-  uint64_t* kv_empty = bars + 1 + 2 * NS;
-  uint64_t* s_full = bars + 1 + 3 * NS;
-  uint64_t* p_full = s_full + TILES;
-  uint64_t* pv_done = p_full + TILES;
+  uint64_t* q_full = bars;                     // [TILES]
+  uint64_t* q_empty = q_full + TILES;          // [TILES]: the item's last QK on Q_t is done
+  uint64_t* k_full = q_empty + TILES;          // [NS]
+  uint64_t* v_full = k_full + NS;              // [NS]
+  uint64_t* kv_empty = v_full + NS;            // [NS]
+  uint64_t* s_full = kv_empty + NS;            // [TILES]
+  uint64_t* p_full = s_full + TILES;           // [TILES]
+  uint64_t* pv_done = p_full + TILES;          // [TILES]
+  uint64_t* item_full = pv_done + TILES;       // [NIS]
+  uint64_t* item_empty = item_full + NIS;      // [NIS]: 9 arrivals (MMA, 8 softmax warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT_OFF);
+  volatile int* item_ids = reinterpret_cast<volatile int*>(smem + L::ITEM_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh % p.H;
-  const int c = p.causal ? (p.num_q_ctas - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int q0 = c * (TILES * BM);
-  const int nkv_all = (p.N + BN - 1) / BN;
-  int nkv_t[TILES];
-#pragma unroll
-  for (int t = 0; t < TILES; ++t) {
-    const int qt0 = q0 + t * BM;
-    nkv_t[t] = qt0 >= p.N ? 0 : (p.causal ? min(nkv_all, qt0 / BN + 1) : nkv_all);
-  }
-  const int nkv = max(nkv_t[0], nkv_t[1]);
+  const int n_items = p.BH * p.num_q_ctas;
+  // Consumer side of the work-item ring: id of the k-th item (>= n_items:
+  // no more work), or -1 when the wait gave up.
+  auto next_item = [&](int k) -> int {
+    const int slot = k % NIS;
+    if (!mbar_wait(&item_full[slot], (k / NIS) & 1, 0x10A)) return -1;
+    const int id = item_ids[slot];
+    mbar_arrive(&item_empty[slot]);
+    return id;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int t = 0; t < TILES; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], BM);
+      mbar_init(&pv_done[t], 1);
+    }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int t = 0; t < TILES; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], BM);
-      mbar_init(&pv_done[t], 1);
+    for (int i = 0; i < NIS; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 9);
     }
     fence_barrier_init();
   }
@@ -157,38 +225,52 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint8_t* sK = smem + L::K_OFF;
   uint8_t* sV = smem + L::V_OFF;
 
-  // Register split: 384 threads x 168 at launch = 128 x 56 (TMA/MMA warpgroup)
-  // + 256 x 224 (softmax warpgroups).
+  // Register split: 384 threads x 168 at launch >= 128 x 96 (TMA/MMA
+  // warpgroup) + 256 x 200 (softmax warpgroups).
   // (setmaxnreg sits at the top of each role's branch so ptxas budgets each.)
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
-    reg_dealloc<56>();
+    reg_dealloc<96>();
     if (lane == 0) {
       prefetch_tmap(&tq); prefetch_tmap(&tk); prefetch_tmap(&tv);
-      mbar_arrive_expect_tx(q_full, TILES * KC * CHUNK_BYTES);
-      for (int t = 0; t < TILES; ++t)
-        for (int kc = 0; kc < KC; ++kc)
-          tma_load_4d(sQ + (t * KC + kc) * CHUNK_BYTES, &tq, q_full, kc * 64, q0 + t * BM, h, b);
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j % NS;
-        if (j >= NS && !mbar_wait(&kv_empty[s], ((j / NS) - 1) & 1, 0x101)) break;
-        mbar_arrive_expect_tx(&k_full[s], KC * CHUNK_BYTES);
-        for (int kc = 0; kc < KC; ++kc)
-          tma_load_4d(sK + (s * KC + kc) * CHUNK_BYTES, &tk, &k_full[s], kc * 64, j * BN, h, b);
-        mbar_arrive_expect_tx(&v_full[s], KC * CHUNK_BYTES);
-        for (int kc = 0; kc < KC; ++kc)
-          tma_load_4d(sV + (s * KC + kc) * CHUNK_BYTES, &tv, &v_full[s], kc * 64, j * BN, h, b);
+      int J = 0;  // running K/V tile count of this CTA
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k % NIS;
+        if (k >= NIS && !mbar_wait(&item_empty[slot], ((k / NIS) - 1) & 1, 0x104)) break;
+        const int item = atomicAdd(p.work_counter, 1);
+        item_ids[slot] = item;
+        mbar_arrive(&item_full[slot]);  // release: the id is visible to its waiters
+        if (item >= n_items) break;
+        const Item w = decode_item(item, p);
+        for (int t = 0; t < TILES; ++t) {
+          if (k > 0 && !mbar_wait(&q_empty[t], (k - 1) & 1, 0x103)) { ok = false; break; }
+          mbar_arrive_expect_tx(&q_full[t], KC * CHUNK_BYTES);
+          for (int kc = 0; kc < KC; ++kc)
+            tma_load_4d(sQ + (t * KC + kc) * CHUNK_BYTES, &tq, &q_full[t], kc * 64,
+                        w.q0 + t * BM, w.h, w.b);
+        }
+        for (int j = 0; ok && j < w.nkv; ++j, ++J) {
+          const int s = J % NS;
+          if (J >= NS && !mbar_wait(&kv_empty[s], ((J / NS) - 1) & 1, 0x101)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[s], KC * CHUNK_BYTES);
+          for (int kc = 0; kc < KC; ++kc)
+            tma_load_4d(sK + (s * KC + kc) * CHUNK_BYTES, &tk, &k_full[s], kc * 64, j * BN, w.h, w.b);
+          mbar_arrive_expect_tx(&v_full[s], KC * CHUNK_BYTES);
+          for (int kc = 0; kc < KC; ++kc)
+            tma_load_4d(sV + (s * KC + kc) * CHUNK_BYTES, &tv, &v_full[s], kc * 64, j * BN, w.h, w.b);
+        }
       }
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
-    reg_dealloc<56>();
+    reg_dealloc<96>();
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = idesc_f16(BM, BN, FMT, 0, 0);
       constexpr uint32_t IDESC_PV = idesc_f16(BM, D, FMT, 0, 1);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      auto issue_qk = [&](int t, int j) {
-        const int s = j % NS;
+      auto issue_qk = [&](int t, int J) {
+        const int s = J % NS;
         const uint32_t d_tmem = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -199,147 +281,181 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
         mma_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
-        const int s = j % NS;
+      auto issue_pv = [&](int t, int J, bool acc) {
+        const int s = J % NS;
         const uint32_t d_tmem = tmem + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bd =
               smem_desc_sw128(v_base + (s * KC) * CHUNK_BYTES + kk * 2048, CHUNK_BYTES, 1024);
-          mma_ts(d_tmem, tmem + t * 128 + kk * 8, bd, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(d_tmem, tmem + t * 128 + kk * 8, bd, IDESC_PV, (acc || kk > 0) ? 1u : 0u);
         }
         mma_commit(&pv_done[t]);
       };
-      bool ok = mbar_wait(q_full, 0, 0x201) && (nkv == 0 || mbar_wait(&k_full[0], 0, 0x202));
-      if (ok) {
+      int J = 0;                     // running K/V tile count
+      int jt[TILES] = {0, 0};        // running K/V step count per query tile
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int item = next_item(k);
+        if (item < 0 || item >= n_items) break;
+        const Item w = decode_item(item, p);
+        for (int t = 0; t < TILES && ok; ++t)
+          if (!mbar_wait(&q_full[t], k & 1, 0x201)) ok = false;
+        if (!ok) break;
+        if (w.nkv > 0 && !mbar_wait(&k_full[J % NS], (J / NS) & 1, 0x202)) { ok = false; break; }
         tc_fence_after();
-        for (int t = 0; t < TILES; ++t)
-          if (nkv_t[t] > 0) issue_qk(t, 0);
-      }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j % NS;
-        if (!mbar_wait(&v_full[s], (j / NS) & 1, 0x203)) { ok = false; break; }
         for (int t = 0; t < TILES; ++t) {
-          if (j >= nkv_t[t]) continue;
-          if (!mbar_wait(&p_full[t], j & 1, 0x204)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < nkv_t[t]) {
-            const int s1 = (j + 1) % NS;
-            // S_t is overwritten by the next QK: wait until PV_t(j) has read P_t.
-            if (!mbar_wait(&k_full[s1], ((j + 1) / NS) & 1, 0x205) ||
-                !mbar_wait(&pv_done[t], j & 1, 0x206)) { ok = false; break; }
-            tc_fence_after();
-            issue_qk(t, j + 1);
-          }
+          if (w.nkv_t[t] > 0) issue_qk(t, J);
+          if (w.nkv_t[t] <= 1) mma_commit(&q_empty[t]);  // last (or no) QK on Q_t
         }
-        mma_commit(&kv_empty[s]);
+        for (int j = 0; ok && j < w.nkv; ++j) {
+          const int s = (J + j) % NS;
+          if (!mbar_wait(&v_full[s], ((J + j) / NS) & 1, 0x203)) { ok = false; break; }
+          for (int t = 0; t < TILES; ++t) {
+            if (j >= w.nkv_t[t]) continue;
+            if (!mbar_wait(&p_full[t], (jt[t] + j) & 1, 0x204)) { ok = false; break; }
+            tc_fence_after();
+            // PV_t(0) of an item overwrites O_t: its softmax warpgroup read
+            // the previous item's O_t out before this p_full.
+            issue_pv(t, J + j, j > 0);
+            if (j + 1 < w.nkv_t[t]) {
+              const int s1 = (J + j + 1) % NS;
+              if (!mbar_wait(&k_full[s1], ((J + j + 1) / NS) & 1, 0x205)) { ok = false; break; }
+              tc_fence_after();
+              issue_qk(t, J + j + 1);
+              if (j + 2 == w.nkv_t[t]) mma_commit(&q_empty[t]);  // last QK on Q_t
+            }
+          }
+          mma_commit(&kv_empty[s]);
+        }
+        J += w.nkv;
+        for (int t = 0; t < TILES; ++t) jt[t] += w.nkv_t[t];
       }
     }
   } else if (warp < 4) {
-    reg_dealloc<56>();  // warps 2-3: idle members of the TMA/MMA warpgroup
+    reg_dealloc<96>();  // warps 2-3: idle members of the TMA/MMA warpgroup
   } else {
     // ------------------------------------------------------------- softmax --
-    reg_alloc<224>();
+    reg_alloc<200>();
     const int t = (warp >> 2) - 1;
     const int row = threadIdx.x - 128 * (t + 1);          // TMEM lane of this thread
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const int qt0 = q0 + t * BM;
-    const int row_g = qt0 + row;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
+    int jt = 0;  // running K/V step count of this query tile
     bool ok = true;
-    for (int j = 0; j < nkv_t[t]; ++j) {
-      if (!mbar_wait_warp(&s_full[t], j & 1, 0x301)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[4][32];
+    for (int k = 0; ok; ++k) {
+      int item = 0;
+      if (lane == 0) item = next_item(k);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item < 0 || item >= n_items) break;
+      const Item w = decode_item(item, p);
+      const int nkv_t = w.nkv_t[t];
+      const int qt0 = w.q0 + t * BM;
+      const int row_g = qt0 + row;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv_t; ++j) {
+        if (!mbar_wait_warp(&s_full[t], (jt + j) & 1, 0x301)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sr[4][32];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tmem_ld32(lane_addr + t * 128 + 32 * i, sr[i]);
-      tmem_ld_wait();
-      const int kv0 = j * BN;
-      // Only the diagonal tile (causal) and the tile holding position N-1 need masks.
-      const bool need_mask = (kv0 + BN > p.N) || (p.causal && kv0 + BN - 1 > qt0);
-      const int lim = min(p.N, p.causal ? row_g + 1 : p.N) - kv0;  // valid columns < lim
-      const float mx = need_mask ? row_max<true>(sr, lim) : row_max<false>(sr, lim);
-      const float m_new = fmaxf(m, mx * sl2);
-      float alpha = 1.f;
-      const bool rescale = m_new > m + RESCALE_THRESHOLD;
-      if (rescale) {
-        alpha = ex2(m - m_new);
-        m = m_new;
-        l *= alpha;
-      }
-      const float m_use = (m == -INFINITY) ? 0.f : m;
-      // Packed f32x2 arithmetic halves the instruction count of the scale and
-      // row-sum steps; the exponentials go to MUFU.EX2.
-      float2 l2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                      make_float2(0.f, 0.f)};
-      const float2 sl2_2 = make_float2(sl2, sl2), negm2 = make_float2(-m_use, -m_use);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i][2 * cc]),
-                                                  __uint_as_float(sr[i][2 * cc + 1])),
-                                      sl2_2, negm2);
-          const float2 pp = make_float2(ex2(x.x), ex2(x.y));
-          l2[cc & 3] = __fadd2_rn(l2[cc & 3], pp);
-          pk[cc] = FMT == 1 ? pack_bf16(pp.x, pp.y) : pack_f16(pp.x, pp.y);
+        for (int i = 0; i < 4; ++i) tmem_ld32(lane_addr + t * 128 + 32 * i, sr[i]);
+        tmem_ld_wait();
+        const int kv0 = j * BN;
+        // Only the diagonal tile (causal) and the tile holding position N-1 need masks.
+        const bool need_mask = (kv0 + BN > p.N) || (p.causal && kv0 + BN - 1 > qt0);
+        const int lim = min(p.N, p.causal ? row_g + 1 : p.N) - kv0;  // valid columns < lim
+        const float mx = need_mask ? row_max<true>(sr, lim) : row_max<false>(sr, lim);
+        const float m_new = fmaxf(m, mx * sl2);
+        float alpha = 1.f;
+        const bool rescale = m_new > m + RESCALE_THRESHOLD;
+        if (rescale) {
+          alpha = ex2(m - m_new);
+          m = m_new;
+          l *= alpha;
         }
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        // Packed f32x2 arithmetic halves the instruction count of the scale and
+        // row-sum steps; the exponentials go to MUFU.EX2.
+        float2 l2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
+        const float2 sl2_2 = make_float2(sl2, sl2), negm2 = make_float2(-m_use, -m_use);
 #pragma unroll
-        for (int cc = 0; cc < 16; ++cc) sr[i >> 1][(i & 1) * 16 + cc] = pk[cc];
+        for (int i = 0; i < 4; ++i) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) {
+            const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i][2 * cc]),
+                                                    __uint_as_float(sr[i][2 * cc + 1])),
+                                        sl2_2, negm2);
+            const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+            l2[cc & 3] = __fadd2_rn(l2[cc & 3], pp);
+            pk[cc] = FMT == 1 ? pack_bf16(pp.x, pp.y) : pack_f16(pp.x, pp.y);
+          }
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) sr[i >> 1][(i & 1) * 16 + cc] = pk[cc];
+        }
+        {
+          const float2 a2 = __fadd2_rn(__fadd2_rn(l2[0], l2[1]), __fadd2_rn(l2[2], l2[3]));
+          l += a2.x + a2.y;
+        }
+        tmem_st32(lane_addr + t * 128, sr[0]);
+        tmem_st32(lane_addr + t * 128 + 32, sr[1]);
+        // tcgen05.ld/st are warp-collective: if any row of the warp rescales,
+        // the whole warp runs the loop (alpha is 1 for rows that do not).
+        // PV_t(j-1) has completed: s_full(j) follows it in issue order.
+        if (__any_sync(0xffffffffu, rescale && j > 0)) {
+          if (!(rescale && j > 0)) alpha = 1.f;
+#pragma unroll
+          for (int i = 0; i < D / 32; ++i) {
+            uint32_t ov[32];
+            tmem_ld32(lane_addr + 256 + t * 128 + 32 * i, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int cc = 0; cc < 32; ++cc) ov[cc] = __float_as_uint(__uint_as_float(ov[cc]) * alpha);
+            tmem_st32(lane_addr + 256 + t * 128 + 32 * i, ov);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
       }
-      {
-        const float2 a2 = __fadd2_rn(__fadd2_rn(l2[0], l2[1]), __fadd2_rn(l2[2], l2[3]));
-        l += a2.x + a2.y;
-      }
-      tmem_st32(lane_addr + t * 128, sr[0]);
-      tmem_st32(lane_addr + t * 128 + 32, sr[1]);
-      // tcgen05.ld/st are warp-collective: if any row of the warp rescales,
-      // the whole warp runs the loop (alpha is 1 for rows that do not).
-      if (__any_sync(0xffffffffu, rescale && j > 0)) {
-        if (!(rescale && j > 0)) alpha = 1.f;
+      if (!ok) break;
+      if (nkv_t > 0) {
+        if (!mbar_wait_warp(&pv_done[t], (jt + nkv_t - 1) & 1, 0x302)) { ok = false; break; }
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
+                        2 * (w.b * p.so_b + w.h * p.so_h + (int64_t)row_g * p.so_n);
+        // Whole 32-byte sectors per store when aligned: with one row per
+        // thread, 16-byte stores reach about half the SM's write bandwidth.
+        const bool st32 = (reinterpret_cast<uintptr_t>(orow) & 31) == 0;
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) {
           uint32_t ov[32];
           tmem_ld32(lane_addr + 256 + t * 128 + 32 * i, ov);
           tmem_ld_wait();
+          uint32_t pk[16];
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) ov[cc] = __float_as_uint(__uint_as_float(ov[cc]) * alpha);
-          tmem_st32(lane_addr + 256 + t * 128 + 32 * i, ov);
+          for (int cc = 0; cc < 16; ++cc) {
+            const float a0 = __uint_as_float(ov[2 * cc]) * inv_l;
+            const float a1 = __uint_as_float(ov[2 * cc + 1]) * inv_l;
+            pk[cc] = FMT == 1 ? pack_bf16(a0, a1) : pack_f16(a0, a1);
+          }
+          if (row_g < p.N && st32) {
+#pragma unroll
+            for (int v8 = 0; v8 < 2; ++v8) st_global_v8(orow + 64 * i + 32 * v8, &pk[8 * v8]);
+          } else if (row_g < p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + 64 * i);
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
+          }
         }
+        if (p.lse != nullptr && row_g < p.N)
+          p.lse[(int64_t)w.bh * p.N + row_g] = (m + __log2f(l)) * 0.6931471805599453f;
+        tc_fence_before();
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
-    }
-    if (ok && nkv_t[t] > 0 && mbar_wait_warp(&pv_done[t], (nkv_t[t] - 1) & 1, 0x302)) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l;
-      uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                      2 * (b * p.so_b + h * p.so_h + (int64_t)row_g * p.so_n);
-#pragma unroll
-      for (int i = 0; i < D / 32; ++i) {
-        uint32_t ov[32];
-        tmem_ld32(lane_addr + 256 + t * 128 + 32 * i, ov);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          const float a0 = __uint_as_float(ov[2 * cc]) * inv_l;
-          const float a1 = __uint_as_float(ov[2 * cc + 1]) * inv_l;
-          pk[cc] = FMT == 1 ? pack_bf16(a0, a1) : pack_f16(a0, a1);
-        }
-        if (row_g < p.N) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + 64 * i);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
-        }
-      }
-      if (p.lse != nullptr && row_g < p.N)
-        p.lse[(int64_t)bh * p.N + row_g] = (m + __log2f(l)) * 0.6931471805599453f;
+      jt += nkv_t;
     }
   }
 
@@ -353,12 +469,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 
 }  // namespace fa_fwd
 
+
 bool attn_fwd_tc_eligible(const void* q, const void* k, const void* v, const void* o, int64_t B,
                           int64_t H, int64_t N, int64_t D, const int64_t* sq, const int64_t* sk,
                           const int64_t* sv, const int64_t* so, int dtype) {
   if (dtype != LSB_DTYPE_BF16 && dtype != LSB_DTYPE_F16) return false;
   if (D != 64 && D != 128) return false;
-  if (B * H > 65535 || N >= (1LL << 30)) return false;
+  if (N >= (1LL << 30) || B * H * ((N + 255) / 256) > 0x7fffffff) return false;
   if (!tma_ok(q, B, H, N, sq, 2) || !tma_ok(k, B, H, N, sk, 2) || !tma_ok(v, B, H, N, sv, 2))
     return false;
   // Output rows are written with 16-byte stores.
@@ -381,15 +498,32 @@ static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   Params p;
   p.o = o; p.lse = lse;
   p.so_b = so[0]; p.so_h = so[1]; p.so_n = so[2];
-  p.H = (int)H; p.N = (int)N;
+  p.H = (int)H; p.N = (int)N; p.BH = (int)(B * H);
   p.num_q_ctas = (int)((N + TILES * BM - 1) / (TILES * BM));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
+  // Work-item counter: a slot of g_work_counters per launch (rotating, so
+  // launches in flight on other streams use other slots), zeroed in stream
+  // order just before the kernel (also when captured into a CUDA graph).
+  static int* counters[64] = {nullptr};
+  int dev = 0;
+  LSB_CUDA_OK(cudaGetDevice(&dev), "attn_fwd_tc device");
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (counters[dev] == nullptr) {
+    void* addr = nullptr;
+    LSB_CUDA_OK(cudaGetSymbolAddress(&addr, g_work_counters), "attn_fwd_tc counter symbol");
+    counters[dev] = static_cast<int*>(addr);
+  }
+  static std::atomic<unsigned> next_slot{0};
+  p.work_counter = counters[dev] + (next_slot.fetch_add(1, std::memory_order_relaxed) % COUNTER_SLOTS);
+  LSB_CUDA_OK(cudaMemsetAsync(p.work_counter, 0, sizeof(int), st), "attn_fwd_tc counter reset");
   const int smem = Smem<D>::ALLOC;
   auto kern = fa_fwd_kernel<D, FMT>;
   LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
               "attn_fwd_tc smem attribute");
-  dim3 grid((unsigned)p.num_q_ctas, (unsigned)(B * H));
+  // Persistent: one CTA per SM (shared memory and TMEM allow no more).
+  const int64_t n_items = B * H * p.num_q_ctas;
+  dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));
   kern<<<grid, THREADS, smem, st>>>(mq, mk, mv, p);
   LSB_CHECK_LAUNCH("attn_fwd_tc");
   return LSB_OK;
