@@ -147,14 +147,29 @@ def time_cuda(fn, steps: int, warmup: int, ws: int):
 
 
 # ---------------------------------------------------------------- workloads --
+def attn_fwd_flops(B, H, N, D, causal: bool) -> float:
+    """lightserve's convention (kernels/benchmark_flash_attention.py:55-64)."""
+    f = 4.0 * B * H * N * N * D
+    return f / 2 if causal else f
+
+
+def attn_bwd_flops(B, H, N, D, causal: bool) -> float:
+    """2.5 x forward (kernels/benchmark_flash_attention_backward.py:59-68)."""
+    return 2.5 * attn_fwd_flops(B, H, N, D, causal)
+
+
+def rmsnorm_bytes(M, N, elem_bytes) -> int:
+    """Read x, residual; write out, h (kernels/benchmark_fused_rmsnorm_residual.py:59-64)."""
+    return 4 * M * N * elem_bytes
+
+
 def _randn(shape, dtype, gen):
     return torch.randn(*shape, device="cuda", dtype=torch.float32, generator=gen).to(dtype)
 
 
 def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
-    from lightserve_b200.kernels import flash_attention_forward
+    from lightserve_b200.kernels import flash_attention_forward, flash_attention_forward_host
     from lightserve_b200.sharding import shard_range
-    from oracle.attention import attn_fwd_flops
 
     c = FWD_CFG
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
@@ -170,15 +185,14 @@ def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
     ms = total_ms / steps
     kern_ms = statistics.mean(per)
 
-    # End to end through the public API: pinned host inputs copied in, output read back.
+    # End to end through the public API with host buffers: pinned q, k, v in
+    # host memory, the output back in host memory (flash_attention_forward_host
+    # streams (b, h) chunks: copies in both directions overlap the kernel).
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     ho = torch.empty_like(hq).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
     def e2e_step():
-        dq.copy_(hq, non_blocking=True); dk.copy_(hk, non_blocking=True); dv.copy_(hv, non_blocking=True)
-        o = flash_attention_forward(dq, dk, dv, causal=True)
-        ho.copy_(o, non_blocking=True)
+        flash_attention_forward_host(hq, hk, hv, causal=True, out=ho, device=q.device)
 
     e2e_total, _ = time_cuda(e2e_step, e2e_steps, 1, ws)
     nb = q.numel() * q.element_size()
@@ -197,7 +211,6 @@ def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
 def bench_bwd(steps, warmup, ws, rank):
     from lightserve_b200.kernels.flash_attention_backward import (_flash_attention_backward,
                                                                   _flash_attention_forward_lse)
-    from oracle.attention import attn_bwd_flops
 
     c = BWD_CFG
     gen = torch.Generator(device="cuda").manual_seed(2000 + rank)
@@ -212,7 +225,6 @@ def bench_bwd(steps, warmup, ws, rank):
 
 def bench_rmsnorm(steps, warmup, ws, rank):
     from lightserve_b200.kernels import fused_add_rmsnorm
-    from oracle.rmsnorm import rmsnorm_bytes
 
     c = RMS_CFG
     gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
@@ -259,6 +271,31 @@ def bench_decode(steps, warmup, ws, rank):
     return {"ms_per_step": ms, "value": ws * c["S"] / (ms * 1e-3), "unit": "tokens/s",
             "hbm_bytes_per_step": kv_bytes + w_bytes, "achieved_gbs": (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9,
             "seqs_per_gpu": c["S"], "mean_prompt": sum(lens) / len(lens)}
+
+
+def bench_torch_sdpa(steps, warmup):
+    """Context, not the product: PyTorch's own scaled_dot_product_attention
+    (whatever backend it dispatches to on this GPU) on config 2 (forward) and
+    config 3 (backward through autograd), same FLOP conventions."""
+    import torch.nn.functional as F
+
+    gen = torch.Generator(device="cuda").manual_seed(4000)
+    c = FWD_CFG
+    q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(3))
+    with torch.no_grad():
+        total, _ = time_cuda(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), steps, warmup, 1)
+    fwd = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
+    del q, k, v
+    c = BWD_CFG
+    q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen).requires_grad_()
+               for _ in range(3))
+    do = _randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    total, _ = time_cuda(lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True),
+                         steps, warmup, 1)
+    bwd = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
+    return {"fwd_tflops": fwd, "bwd_tflops": bwd,
+            "note": "torch.nn.functional.scaled_dot_product_attention, bf16, causal; context only"}
 
 
 # ------------------------------------------------------------- CPU baseline --
@@ -328,7 +365,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--only", default="fwd,bwd,rmsnorm,decode",
+    ap.add_argument("--only", default="fwd,bwd,rmsnorm,decode,context",
                     help="comma list of workloads (fwd is always run: it is the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--strong", action="store_true",
@@ -354,6 +391,11 @@ def main():
         secondary["rmsnorm"]["frac_of_peak"] = secondary["rmsnorm"]["value"] / ws / peaks["hbm_gbs"]
     if "decode" in only:
         secondary["paged_decode"] = bench_decode(min(args.steps * 4, 128), args.warmup, ws, rank)
+    if ws == 1 and "context" in only:
+        try:
+            secondary["torch_sdpa_context"] = bench_torch_sdpa(args.steps, args.warmup)
+        except Exception as e:  # context only: never fail the bench on it
+            secondary["torch_sdpa_context"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     if rank != 0:
         return
     cpu = None

@@ -169,6 +169,16 @@ LSB_API int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, int6
                               void* stream);
 
 /*
+ * Fused SwiGLU of the Llama MLP: out = silu(gate) * up with
+ * gate = gu[:, :I], up = gu[:, I:] (gu = [S, 2I], the fused gate|up GEMM
+ * output, row stride ld_gu; out = [S, I], row stride ld_out). Replaces
+ * F.silu(gate_proj(h)) * up_proj(h) (model/minimal_llama.py:231-233) with the
+ * same roundings: silu in fp32 rounded to dtype, then the dtype product.
+ */
+LSB_API int lsb_swiglu(const void* gu, void* out, int64_t S, int64_t I, int64_t ld_gu,
+                       int64_t ld_out, int dtype, void* stream);
+
+/*
  * Allocation-free paged decode. No counterpart exists in lightserve: this is
  * lsb_paged_decode for callers that cannot allocate device memory (runtimes
  * whose own pool owns the GPU's memory, FFI bindings without access to the

@@ -57,6 +57,7 @@ SIGNATURES = {
                               _I64, _I64, _I64, _I64, _F, _I, _P, _I64, _P]),
     "lsb_rope_kv_write": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P,
                                _I64, _I64, _I64, _I64, _I64, _I, _P]),
+    "lsb_swiglu": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_paged_decode_static_scratch_capacity": (_I64, []),
     "lsb_paged_decode_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                              _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),

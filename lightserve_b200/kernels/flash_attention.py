@@ -54,3 +54,67 @@ def flash_attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     o = torch.empty_like(q)
     _attn_fwd(q, k, v, o, None, causal)
     return o
+
+
+def flash_attention_forward_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                 causal: bool = False, out: torch.Tensor | None = None,
+                                 device: torch.device | str = "cuda",
+                                 chunk_slices: int = 16) -> torch.Tensor:
+    """flash_attention_forward for q, k, v held in (pinned) host memory.
+
+    The (batch, head) slices stream through the GPU in chunks of
+    ``chunk_slices``: host-to-device copies, the attention kernel and the
+    device-to-host copy of the output run on three streams, double-buffered,
+    so the copies in both directions overlap each other and the compute.
+    Returns ``out`` (default: a new pinned host tensor like ``q``). The
+    calling stream of ``device`` waits for the last copy."""
+    assert q.ndim == 4 and q.shape == k.shape == v.shape, "expected q/k/v as [B, H, N, D] of one shape"
+    assert q.device.type == k.device.type == v.device.type == "cpu", "host tensors expected"
+    assert q.dtype == k.dtype == v.dtype, f"dtype mismatch: q={q.dtype} k={k.dtype} v={v.dtype}"
+    assert q.is_contiguous() and k.is_contiguous() and v.is_contiguous(), "contiguous host tensors expected"
+    assert chunk_slices >= 1
+    _lib.dtype_code(q.dtype)
+    B, H, N, D = q.shape
+    BH = B * H
+    dev = torch.device(device)
+    if out is None:
+        out = torch.empty_like(q).pin_memory()
+    assert out.shape == q.shape and out.dtype == q.dtype and out.is_contiguous()
+    if BH == 0 or N == 0:
+        return out
+    hq, hk, hv, ho = (t.view(BH, N, D) for t in (q, k, v, out))
+    cs = min(chunk_slices, BH)
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_comp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    for s in (s_in, s_comp, s_out):
+        s.wait_stream(cur)
+    nbuf = 2
+    bufs = [[torch.empty(cs, N, D, dtype=q.dtype, device=dev) for _ in range(4)] for _ in range(nbuf)]
+    in_done = [torch.cuda.Event() for _ in range(nbuf)]
+    comp_done = [torch.cuda.Event() for _ in range(nbuf)]
+    out_done = [torch.cuda.Event() for _ in range(nbuf)]
+    for ci, s0 in enumerate(range(0, BH, cs)):
+        bi, n = ci % nbuf, min(cs, BH - s0)
+        dq, dk, dv, do = bufs[bi]
+        with torch.cuda.stream(s_in):
+            if ci >= nbuf:
+                s_in.wait_event(comp_done[bi])  # chunk ci - nbuf has read its inputs
+            for d, h in ((dq, hq), (dk, hk), (dv, hv)):
+                d[:n].copy_(h[s0:s0 + n], non_blocking=True)
+            in_done[bi].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(in_done[bi])
+            if ci >= nbuf:
+                s_comp.wait_event(out_done[bi])  # its output buffer has been copied out
+            x = [t[:n].unsqueeze(0) for t in (dq, dk, dv, do)]
+            _attn_fwd(x[0], x[1], x[2], x[3], None, causal)
+            comp_done[bi].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done[bi])
+            ho[s0:s0 + n].copy_(do[:n], non_blocking=True)
+            out_done[bi].record(s_out)
+    cur.wait_stream(s_out)
+    for bl in bufs:  # keep the device buffers alive until the streams are done with them
+        for t in bl:
+            t.record_stream(s_in); t.record_stream(s_comp); t.record_stream(s_out)
+    return out

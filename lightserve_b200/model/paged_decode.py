@@ -30,6 +30,7 @@ import torch.nn.functional as F
 
 from ..engine import BlockManager, Request
 from ..kernels.fused_rmsnorm_residual import fused_add_rmsnorm
+from ..kernels.fused_swiglu import silu_and_mul
 from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
                                         rope_kv_write, write_kv_cache)
 from .minimal_llama import LlamaConfig, LlamaWeights, llama_forward, precompute_rope
@@ -84,6 +85,7 @@ class PagedDecoder:
         self.zeros = torch.zeros(S, Hd, dtype=config.dtype, device=dev)
         self.attn_out = torch.empty(S, H, D, dtype=config.dtype, device=dev)
         self.q_rot = torch.empty(S, H, D, dtype=config.dtype, device=dev)
+        self.act = torch.empty(S, config.intermediate_size, dtype=config.dtype, device=dev)
         self.ws = paged_decode_workspace((S, H, D), max_blocks_per_seq, cache.block_size, dev)
         self.graph = None
         self.requests: list = []
@@ -151,7 +153,7 @@ class PagedDecoder:
             normed2, residual = fused_add_rmsnorm(x, residual, layer.post_attention_layernorm_weight,
                                                   eps=cfg.rms_eps)
             gu = normed2 @ fz.w_gu
-            x = (F.silu(gu[:, :I]) * gu[:, I:]) @ layer.down_proj
+            x = silu_and_mul(gu, out=self.act) @ layer.down_proj
         final, _ = fused_add_rmsnorm(x, residual, self.w.norm_weight, eps=cfg.rms_eps)
         logits = final @ self.w.lm_head
         nxt = logits.argmax(-1)

@@ -150,3 +150,19 @@ def test_full_size_forward_properties():
     k2 = k.clone(); k2[:, :, -1] += 1.0
     o2 = flash_attention_forward(q, k2, v, causal=True)
     assert torch.equal(o[:, :, :-1], o2[:, :, :-1])
+
+
+@pytest.mark.parametrize("chunk", [1, 3, 16])
+def test_forward_host_streaming_matches_device(chunk):
+    """flash_attention_forward_host streams (b, h) chunks of pinned host
+    tensors through the same kernel: bit-identical to the device call."""
+    from lightserve_b200.kernels import flash_attention_forward_host
+
+    torch.manual_seed(5)
+    B, H, N, D = 2, 5, 300, 128
+    q, k, v = (torch.randn(B, H, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(3))
+    got = flash_attention_forward_host(q, k, v, causal=True, chunk_slices=chunk)
+    torch.cuda.synchronize()
+    want = flash_attention_forward(q.cuda(), k.cuda(), v.cuda(), causal=True).cpu()
+    assert got.device.type == "cpu"
+    torch.testing.assert_close(got, want, atol=0, rtol=0)

@@ -61,3 +61,18 @@ def test_paged_decode_rejects_bad_tables():
     kc = torch.randn(8, 4, 16, 64)
     with pytest.raises(AssertionError):
         paged_decode_attention(q, kc, kc, torch.zeros(2, 4, dtype=torch.int64), torch.ones(2, dtype=torch.int32))
+
+
+def test_swiglu_rejects_bad_input():
+    from lightserve_b200.kernels import silu_and_mul
+    with pytest.raises(AssertionError):
+        silu_and_mul(torch.zeros(4, 6))  # CPU tensor
+    with pytest.raises(AssertionError):
+        silu_and_mul(torch.zeros(4, 5, device="meta"))  # odd width
+
+
+def test_forward_host_rejects_device_tensors():
+    from lightserve_b200.kernels import flash_attention_forward_host
+    q = torch.zeros(1, 1, 4, 8, device="meta")
+    with pytest.raises(AssertionError):
+        flash_attention_forward_host(q, q, q)
