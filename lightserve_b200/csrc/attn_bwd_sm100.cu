@@ -20,7 +20,9 @@
 //   [384,512) dP^T = V dO^T    (SS MMA), then dQ^T = K^T dS^T (SS MMA, K^T
 //             read MN-major from the K tile, dS^T from a 128-byte-swizzled
 //             shared tile)
-// Warp 0 streams K/V once, Q tiles (plus each tile's log-sum-exp and Dsum)
+// Warp 0 streams K/V once per item (V reloaded once the item's last dP^T is
+// done, K once its last dQ^T is done, both prefetched into L2 when the item
+// is claimed during the previous item's last tile), Q tiles (plus each tile's log-sum-exp and Dsum)
 // through a 2-stage ring and dO tiles through one buffer (dO(i+1) loads
 // while dQ(i), dK(i) and S(i+1) run); warp 1 owns TMEM and issues the MMAs
 // in the order dV(i), dQ(i), dK(i), S(i+1), dP(i+1); warp 2 adds the finished
@@ -75,11 +77,12 @@ constexpr int STAGE_ROWS = 64;                  // dQ rows per staging buffer (6
 static_assert(STAGE_ROWS * D * 4 == TILE, "a dQ staging buffer holds half a query tile");
 constexpr int STAT_OFF = STG_OFF + TILE;        // [NQS][2][BM] floats: lse2, dsum
 constexpr int BAR_OFF = STAT_OFF + NQS * 2 * BM * 4;
-// kv_full, kv_empty, q_full[NQS], q_empty[NQS], stat_full[NQS], do_full, do_empty,
+// k_full, v_full, k_empty, q_full[NQS], q_empty[NQS], stat_full[NQS], do_full, do_empty,
 // s_ready, p_ready, dp_ready, ds_ready, dq_ready, dq_free, dk_done, red_full[2],
-// red_free[2], item_full[NIS], item_empty[NIS]
+// red_free[2], epi_staged, epi_v_free, vdo_issued, epi_q_free[NQS], item_full[NIS],
+// item_empty[NIS]
 constexpr int NIS = 4;    // work-item id ring slots
-constexpr int NBAR = 2 + 3 * NQS + 13 + 2 * NIS;
+constexpr int NBAR = 3 + 4 * NQS + 16 + 2 * NIS;
 constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
 constexpr int ITEM_OFF = SLOT_OFF + 16;         // [NIS] work-item ids
 constexpr int SMEM = ITEM_OFF + NIS * 4;
@@ -96,20 +99,10 @@ struct Params {
   const float* dsum;
   float* dq_acc;
   int* work_counter;  // zeroed before launch; CTAs take work items from it
-  void* dk;
-  void* dv;
-  int64_t sdk_b, sdk_h, sdk_n, sdv_b, sdv_h, sdv_n;
   int H, N, BH;
   float scale, scale_log2;
   int causal;
 };
-
-// 32-byte global store (sm_100 256-bit vector store); dst 32-byte aligned.
-__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* w) {
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
-               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-               : "memory");
-}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -177,12 +170,13 @@ __device__ __forceinline__ Item decode_item(int item, const Params& p) {
 // from p.work_counter and passes the id to the other roles through a small
 // ring (item_full / item_empty); id >= n_items ends every role's loop. Every
 // per-tile barrier completes once per query tile, so its phase is the
-// CTA-wide running tile count g (across items), and kv_full / kv_empty
-// complete once per item.
+// CTA-wide running tile count g (across items), and k_full / v_full /
+// k_empty / epi_staged / epi_v_free complete once per item.
 template <int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
               const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+              const __grid_constant__ CUtensorMap tdk, const __grid_constant__ CUtensorMap tdv,
               const Params p) {
   // No static shared memory is declared, so the dynamic block starts at the
   // (1 KiB-aligned) base of the CTA's window; the 128-byte swizzle needs
@@ -193,9 +187,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = kv_full + 1;            // the item's last MMA has read K and V
-  uint64_t* q_full = kv_empty + 1;             // [NQS]
+  uint64_t* k_full = bars;
+  uint64_t* v_full = k_full + 1;
+  uint64_t* k_empty = v_full + 1;              // the item's last dQ^T MMA (last reader of K) is done
+  uint64_t* q_full = k_empty + 1;              // [NQS]
   uint64_t* q_empty = q_full + NQS;            // [NQS]
   uint64_t* stat_full = q_empty + NQS;         // [NQS]: log-sum-exp / Dsum staged
   uint64_t* do_full = stat_full + NQS;
@@ -213,7 +208,22 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint64_t* red_full = dk_done + 1;            // [2]
   uint64_t* red_free = red_full + 2;           // [2]
   float* stats = reinterpret_cast<float*>(smem + STAT_OFF);  // [NQS][lse2 BM | dsum BM]
-  uint64_t* item_full = red_free + 2;          // [NIS]
+  // Item epilogue: the warpgroups stage dK in the V buffer and dV in the Q
+  // stage of the item's last tile as bf16 tiles (epi_staged, 256
+  // arrivals); the reducer stores both with TMA ahead of the item's last dQ
+  // reduction. epi_v_free (once per item) and epi_q_free[stage] (once per
+  // staging in that stage) tell the producer that a buffer has been read;
+  // the next item's first dP^T waits for V, its second S^T for the Q stage.
+  uint64_t* epi_staged = red_free + 2;
+  uint64_t* epi_v_free = epi_staged + 1;
+  // The producer has issued the next item's V and dO loads (once per item;
+  // after the CTA's last item, with nothing to load): the reducer issues
+  // the last tile's dQ reductions only then, since the TMA unit serves its
+  // bulk operations in order and the loads would otherwise wait for 64 KiB
+  // of reduction traffic.
+  uint64_t* vdo_issued = epi_v_free + 1;
+  uint64_t* epi_q_free = vdo_issued + 1;       // [NQS]
+  uint64_t* item_full = epi_q_free + NQS;      // [NIS]
   uint64_t* item_empty = item_full + NIS;      // [NIS]: 10 arrivals (MMA, reducer, 8 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SLOT_OFF);
   volatile int* item_ids = reinterpret_cast<volatile int*>(smem + ITEM_OFF);
@@ -231,8 +241,9 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   };
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(kv_empty, 1);
+    mbar_init(k_full, 1);
+    mbar_init(v_full, 1);
+    mbar_init(k_empty, 1);
     for (int s = 0; s < NQS; ++s) {
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
@@ -248,6 +259,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     mbar_init(dq_free, 256);
     mbar_init(dk_done, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&red_full[i], 128); mbar_init(&red_free[i], 1); }
+    mbar_init(epi_staged, 256);
+    mbar_init(epi_v_free, 1);
+    mbar_init(vdo_issued, 1);
+    for (int i = 0; i < NQS; ++i) mbar_init(&epi_q_free[i], 1);
     for (int i = 0; i < NIS; ++i) { mbar_init(&item_full[i], 1); mbar_init(&item_empty[i], 10); }
     fence_barrier_init();
   }
@@ -272,29 +287,53 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     reg_dealloc<112>();
     if (lane == 0) {
       prefetch_tmap(&tq); prefetch_tmap(&tk); prefetch_tmap(&tv); prefetch_tmap(&tdo);
+      prefetch_tmap(&tdk); prefetch_tmap(&tdv);
     }
     int g = 0;  // running query-tile count of this CTA
     bool ok = true;
-    for (int k = 0; ok; ++k) {
+    // Claims work item k: takes the next id from the global counter and
+    // publishes it in ring slot k % NIS (once item k - NIS has been taken
+    // by every role). The id of item k+1 is claimed while item k's last
+    // query tile loads, and its K / V tiles are prefetched into L2 then, so
+    // the K / V loads at the item boundary read L2 instead of HBM.
+    auto claim = [&](int k) -> int {
       const int slot = k % NIS;
-      if (k >= NIS && !mbar_wait_warp(&item_empty[slot], ((k / NIS) - 1) & 1, 0x504)) break;
-      int item = 0;
+      if (k >= NIS && !mbar_wait_warp(&item_empty[slot], ((k / NIS) - 1) & 1, 0x504)) return -1;
+      int id = 0;
       if (lane == 0) {
-        item = atomicAdd(p.work_counter, 1);
-        item_ids[slot] = item;
+        id = atomicAdd(p.work_counter, 1);
+        item_ids[slot] = id;
         mbar_arrive(&item_full[slot]);  // release: the id is visible to its waiters
+        if (id < n_items) {
+          const Item nw = decode_item(id, p);
+          for (int kc = 0; kc < KC; ++kc) {
+            tma_prefetch_l2_4d(&tk, kc * 64, nw.kv0, nw.h, nw.b);
+            tma_prefetch_l2_4d(&tv, kc * 64, nw.kv0, nw.h, nw.b);
+          }
+        }
       }
-      item = __shfl_sync(0xffffffffu, item, 0);
-      if (item >= n_items) break;
+      return __shfl_sync(0xffffffffu, id, 0);
+    };
+    uint32_t q_pend = 0, q_phase = 0;  // per Q stage: dV staging pending / its phase
+    int item = claim(0);
+    for (int k = 0; ok && item >= 0 && item < n_items; ++k) {
       const Item w = decode_item(item, p);
       BWD_ITEM(item, 0, gtimer());
       const float* lse_bh = p.lse + (int64_t)w.bh * p.N;
       const float* dsum_bh = p.dsum + (int64_t)w.bh * p.N;
+      int next = -1;
       for (int it = 0; it < w.n; ++it, ++g) {
         const int s = g % NQS;
         // Stage s is reused once the MMAs of tile g-NQS (and so every read of
         // its statistics, which precede ds_ready) have completed.
         if (g >= NQS && !mbar_wait_warp(&q_empty[s], ((g / NQS) - 1) & 1, 0x501)) { ok = false; break; }
+        // Tile g-NQS ended an item: its dV staging in this stage must have
+        // been stored first.
+        if ((q_pend >> s) & 1) {
+          if (!mbar_wait_warp(&epi_q_free[s], (q_phase >> s) & 1, 0x506)) { ok = false; break; }
+          q_phase ^= 1u << s;
+          q_pend &= ~(1u << s);
+        }
         const int m0 = (w.i0 + it) * BM;
         if (lane == 0) {
           mbar_arrive_expect_tx(&q_full[s], TILE);
@@ -311,27 +350,42 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           st[BM + c] = in ? __ldg(dsum_bh + m0 + c) : 0.f;
         }
         mbar_arrive(&stat_full[s]);
-        // dO(g) replaces dO(g-1) once dV(g-1) has read it.
+        BWD_TRACE(lane == 0, 0, g);
+        // K of this item replaces the previous item's once its last dQ^T
+        // (the last reader of K) has completed.
+        if (it == 0) {
+          if (k > 0 && !mbar_wait_warp(k_empty, (k - 1) & 1, 0x507)) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(k_full, TILE);
+            for (int kc = 0; kc < KC; ++kc)
+              tma_load_4d(sK + kc * CHUNK, &tk, k_full, kc * 64, w.kv0, w.h, w.b);
+          }
+        }
+        // V replaces the previous item's dK staging once its TMA store has
+        // read it (which follows every MMA of that item); dO(g) replaces
+        // dO(g-1) once dV(g-1) has read it.
+        if (it == 0 && k > 0 && !mbar_wait_warp(epi_v_free, (k - 1) & 1, 0x503)) { ok = false; break; }
         if (g > 0 && !mbar_wait_warp(do_empty, (g - 1) & 1, 0x502)) { ok = false; break; }
+        BWD_TRACE(lane == 0, 3, g);
         if (lane == 0) {
+          if (it == 0) {
+            mbar_arrive_expect_tx(v_full, TILE);
+            for (int kc = 0; kc < KC; ++kc)
+              tma_load_4d(sV + kc * CHUNK, &tv, v_full, kc * 64, w.kv0, w.h, w.b);
+          }
           mbar_arrive_expect_tx(do_full, TILE);
           for (int kc = 0; kc < KC; ++kc)
             tma_load_4d(sDO + kc * CHUNK, &tdo, do_full, kc * 64, m0, w.h, w.b);
+          if (it == 0 && k > 0) mbar_arrive(vdo_issued);
         }
-        // K / V of this item replace the previous item's once all its MMAs
-        // are done (after this item's first Q and dO are on their way).
-        if (it == 0) {
-          if (k > 0 && !mbar_wait_warp(kv_empty, (k - 1) & 1, 0x503)) { ok = false; break; }
-          if (lane == 0) {
-            mbar_arrive_expect_tx(kv_full, 2 * TILE);
-            for (int kc = 0; kc < KC; ++kc) {
-              tma_load_4d(sK + kc * CHUNK, &tk, kv_full, kc * 64, w.kv0, w.h, w.b);
-              tma_load_4d(sV + kc * CHUNK, &tv, kv_full, kc * 64, w.kv0, w.h, w.b);
-            }
-          }
+        if (it == w.n - 1) {
+          q_pend |= 1u << s;
+          next = claim(k + 1);
         }
       }
+      item = next;
     }
+    if (ok && item >= n_items && lane == 0) mbar_arrive(vdo_issued);  // for the CTA's last item
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issue --
     reg_dealloc<112>();
@@ -364,15 +418,18 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       };
       // S^T(g) and dP^T(g). dP^T overwrites dQ^T(g-1) once the warpgroups
       // have loaded it (dq_free).
-      auto issue_s_dp = [&](int gg) -> bool {
+      // An item's first tile also waits for its K (before S^T) and V (before
+      // dP^T).
+      auto issue_s_dp = [&](int gg, int k, bool first) -> bool {
         const int s = gg % NQS;
+        if (first && !mbar_wait(k_full, k & 1, 0x601)) return false;
         if (!mbar_wait(&q_full[s], (gg / NQS) & 1, 0x605)) return false;
         tc_fence_after();
         issue_t(T_S, k_base, q_base + s * TILE);
         mma_commit(s_ready);
         BWD_TRACE(true, 1, gg);
         if ((gg > 0 && !mbar_wait(dq_free, (gg - 1) & 1, 0x606)) ||
-            !mbar_wait(do_full, gg & 1, 0x608))
+            !mbar_wait(do_full, gg & 1, 0x608) || (first && !mbar_wait(v_full, k & 1, 0x609)))
           return false;
         tc_fence_after();
         issue_t(T_DP, v_base, do_base);
@@ -386,9 +443,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         const int item = next_item(k, true);
         if (item < 0 || item >= n_items) break;
         const Item w = decode_item(item, p);
-        if (!mbar_wait(kv_full, k & 1, 0x601)) { ok = false; break; }
-        tc_fence_after();
-        if (!issue_s_dp(g)) { ok = false; break; }
+        if (!issue_s_dp(g, k, true)) { ok = false; break; }
         for (int it = 0; it < w.n; ++it, ++g) {
           const int s = g % NQS;
           const uint32_t ph = g & 1;
@@ -411,6 +466,7 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             mma_ss(tmem + T_DP, a, bd, ID_DQ, kk > 0);
           }
           mma_commit(dq_ready);
+          if (it + 1 == w.n) mma_commit(k_empty);  // the item's last read of K
           issue_acc(T_DK, 32, q_base + s * TILE, it > 0);
           mma_commit(dk_done);
           mma_commit(&q_empty[s]);
@@ -418,16 +474,18 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           // tcgen05.mma instructions of one thread execute in issue order, so
           // S^T(g+1) overwrites P^T / dS^T(g) only after dV(g) and dK(g)
           // have read them.
-          if (it + 1 < w.n && !issue_s_dp(g + 1)) { ok = false; break; }
+          if (it + 1 < w.n && !issue_s_dp(g + 1, k, false)) { ok = false; break; }
         }
-        mma_commit(kv_empty);  // every MMA of this item (all reads of K, V) done
       }
     }
   } else if (warp == 2) {
     // ---------------------------------------------------------- dQ reducer --
     // Adds each staged 64-row dQ half-tile into the fp32 dQ buffer (rows are
     // contiguous there) with one bulk reduction per half; the dS^T-tile half
-    // goes first, since the next dS^T write waits for it to be read.
+    // goes first, since the next dS^T write waits for it to be read. An
+    // item's last tile first hands the item's staged dK and dV tiles to TMA
+    // stores, whose buffers are released once read, and lets the next
+    // item's V / dO loads go ahead of its reductions (vdo_issued).
     reg_dealloc<112>();
     if (lane == 0) {
       int g = 0;
@@ -439,26 +497,47 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         for (int it = 0; it < w.n; ++it, ++g) {
           const uint32_t ph = g & 1;
           const int64_t m0 = (int64_t)(w.i0 + it) * BM;
+          const bool last = it + 1 == w.n;
+          if (last) {
+            // dK store, V buffer released, next V / dO loads issued, then the
+            // dV store and this tile's reductions (every earlier bulk group
+            // has been read by now).
+            ok = mbar_wait(epi_staged, kk & 1, 0x902);
+            if (!ok) break;
+            BWD_TRACE(true, 13, g);
+            for (int kc = 0; kc < KC; ++kc)
+              tma_store_4d(&tdk, sV + kc * CHUNK, kc * 64, w.kv0, w.h, w.b);
+            bulk_commit();
+            bulk_wait_read();
+            mbar_arrive(epi_v_free);
+            BWD_TRACE(true, 14, g);
+            ok = mbar_wait(vdo_issued, kk & 1, 0x903);
+            if (!ok) break;
+            for (int kc = 0; kc < KC; ++kc)
+              tma_store_4d(&tdv, sQ + (g % NQS) * TILE + kc * CHUNK, kc * 64, w.kv0, w.h, w.b);
+            bulk_commit();
+          }
           for (int k = 1; k >= 0 && ok; --k) {
             ok = mbar_wait(&red_full[k], ph, 0x901);
             const int rows = (int)min((int64_t)STAGE_ROWS, p.N - (m0 + k * STAGE_ROWS));
-#ifdef LSB_BWD_NORED
-            if (false)
-#else
             if (ok && rows > 0)
-#endif
               bulk_reduce_add_f32(p.dq_acc + ((int64_t)w.bh * p.N + m0 + k * STAGE_ROWS) * D,
                                   reinterpret_cast<const float*>(k ? sDS : sSTG), rows * D * 4);
             bulk_commit();  // an empty group when nothing was issued
           }
           if (!ok) break;
+          if (last) {
+            bulk_wait_read_2();
+            mbar_arrive(&epi_q_free[g % NQS]);
+            BWD_TRACE(true, 15, g);
+          }
           bulk_wait_read_1();
           mbar_arrive(&red_free[1]);
           bulk_wait_read();
           mbar_arrive(&red_free[0]);
         }
       }
-      bulk_wait_all();  // every reduction has landed before the CTA exits
+      bulk_wait_all();  // every store and reduction has landed before the CTA exits
     }
   } else if (warp < 4) {
     reg_dealloc<112>();
@@ -581,19 +660,18 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         BWD_TRACE(r == 0 && half == 0, 12, g);
       }
       if (!ok) break;
-      // Item epilogue: warpgroup 1 writes this key's dV row, warpgroup 2 its
-      // dK row. The next item's dV(0) / dK(0) overwrite these columns only
-      // after this warpgroup's p_ready of that tile.
+      // Item epilogue: warpgroup 1 stages this key's dV row (in the last
+      // tile's Q stage), warpgroup 2 its dK row (in the V buffer); dk_done:
+      // every MMA of the item, so also the last readers of Q and V, has
+      // completed. The next item's dV(0) / dK(0) overwrite
+      // these columns only after this warpgroup's p_ready of that tile.
       if (!mbar_wait_warp(dk_done, (g - 1) & 1, 0x707)) { ok = false; break; }
       tc_fence_after();
-      // tcgen05.ld is warp-collective: every lane loads, only valid keys store.
-      const bool store = key < p.N;
+      // Staged as bf16 in the TMA store layout ([2 chunks][128 keys][64 d],
+      // 128-byte swizzle); the store skips keys past the sequence end.
       const uint32_t col = half == 0 ? T_DV : T_DK;
       const float mul = half == 0 ? 1.f : p.scale;
-      uint8_t* dst = half == 0
-          ? reinterpret_cast<uint8_t*>(p.dv) + 2 * (w.b * p.sdv_b + w.h * p.sdv_h + (int64_t)key * p.sdv_n)
-          : reinterpret_cast<uint8_t*>(p.dk) + 2 * (w.b * p.sdk_b + w.h * p.sdk_h + (int64_t)key * p.sdk_n);
-      const bool st32 = (reinterpret_cast<uintptr_t>(dst) & 31) == 0;
+      uint8_t* rowp0 = (half == 0 ? sQ + ((g - 1) % NQS) * TILE : sV) + r * 128;
 #pragma unroll
       for (int i = 0; i < D / 32; ++i) {
         uint32_t v[32];
@@ -603,19 +681,17 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
 #pragma unroll
         for (int cc = 0; cc < 16; ++cc)
           pk2[cc] = pack2<FMT>(__uint_as_float(v[2 * cc]) * mul, __uint_as_float(v[2 * cc + 1]) * mul);
-        if (store && st32) {
-          // Whole 32-byte sectors per store: with one key row per thread,
-          // 16-byte stores reach about half the SM's write bandwidth.
+        uint8_t* rowp = rowp0 + (i >> 1) * CHUNK;
 #pragma unroll
-          for (int v8 = 0; v8 < 2; ++v8) st_global_v8(dst + 64 * i + 32 * v8, &pk2[8 * v8]);
-        } else if (store) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 64 * i);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            d4[v4] = make_uint4(pk2[4 * v4], pk2[4 * v4 + 1], pk2[4 * v4 + 2], pk2[4 * v4 + 3]);
+        for (int j = 0; j < 4; ++j) {
+          const int unit = (i & 1) * 4 + j;  // 16-byte unit inside the 128-byte row segment
+          *reinterpret_cast<uint4*>(rowp + ((unit ^ (r & 7)) << 4)) =
+              make_uint4(pk2[4 * j], pk2[4 * j + 1], pk2[4 * j + 2], pk2[4 * j + 3]);
         }
       }
+      fence_proxy_async_smem();
       tc_fence_before();
+      mbar_arrive(epi_staged);
       if (r == 0 && half == 0) BWD_ITEM(item, 2, gtimer());
 #ifdef LSB_BWD_TRACE
       if (r == 0 && half == 0) {
@@ -652,13 +728,8 @@ bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const voi
   if (!tma_ok(q, B, H, N, sq, 2) || !tma_ok(k, B, H, N, sk, 2) || !tma_ok(v, B, H, N, sv, 2) ||
       !tma_ok(dout, B, H, N, sdo, 2))
     return false;
-  // dK/dV rows are written with 16-byte stores.
-  for (auto pr : {std::make_pair(dk, sdk), std::make_pair(dv, sdv)}) {
-    const int64_t* s = pr.second;
-    if (!aligned16(pr.first) || s[3] != 1 || (s[2] * 2) % 16 || (s[1] * 2) % 16 || (s[0] * 2) % 16)
-      return false;
-  }
-  return true;
+  // dK and dV are written with TMA stores.
+  return tma_ok(dk, B, H, N, sdk, 2) && tma_ok(dv, B, H, N, sdv, 2);
 }
 
 template <int FMT>
@@ -669,17 +740,17 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
                          int causal, int dtype, const float* dsum, float* dq_acc,
                          int* work_counter, cudaStream_t st) {
   using namespace fa_bwd;
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdk, mdv;
   int rc = make_bhnd_map(&mq, q, dtype, B, H, N, D, sq, 64, BM);
   if (!rc) rc = make_bhnd_map(&mdo, dout, dtype, B, H, N, D, sdo, 64, BM);
   if (!rc) rc = make_bhnd_map(&mk, k, dtype, B, H, N, D, sk, 64, BN);
   if (!rc) rc = make_bhnd_map(&mv, v, dtype, B, H, N, D, sv, 64, BN);
+  if (!rc) rc = make_bhnd_map(&mdk, dk, dtype, B, H, N, D, sdk, 64, BN);
+  if (!rc) rc = make_bhnd_map(&mdv, dv, dtype, B, H, N, D, sdv, 64, BN);
   if (rc) return rc;
   Params p;
-  p.lse = lse; p.dsum = dsum; p.dq_acc = dq_acc; p.dk = dk; p.dv = dv;
+  p.lse = lse; p.dsum = dsum; p.dq_acc = dq_acc;
   p.work_counter = work_counter;
-  p.sdk_b = sdk[0]; p.sdk_h = sdk[1]; p.sdk_n = sdk[2];
-  p.sdv_b = sdv[0]; p.sdv_h = sdv[1]; p.sdv_n = sdv[2];
   p.H = (int)H; p.N = (int)N; p.BH = (int)(B * H);
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
@@ -690,7 +761,7 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
   // Persistent: one CTA per SM (shared memory and TMEM allow no more).
   const int64_t n_items = B * H * ((N + BN - 1) / BN);
   dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));
-  kern<<<grid, THREADS, SMEM, st>>>(mq, mk, mv, mdo, p);
+  kern<<<grid, THREADS, SMEM, st>>>(mq, mk, mv, mdo, mdk, mdv, p);
   LSB_CHECK_LAUNCH("attn_bwd_tc");
   return LSB_OK;
 }

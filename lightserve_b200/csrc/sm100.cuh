@@ -91,6 +91,27 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Tiled store shared -> global, tracked by the issuing thread's bulk-async
+// group; rows outside the tensor are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// Brings a tile into L2 ahead of its shared-memory load (no completion signal).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
@@ -120,6 +141,10 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Wait until all but the most recent committed bulk group have finished reading.
 __device__ __forceinline__ void bulk_wait_read_1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+// Wait until all but the two most recent committed bulk groups have finished reading.
+__device__ __forceinline__ void bulk_wait_read_2() {
+  asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory");
 }
 // Wait until every committed bulk group has completed.
 __device__ __forceinline__ void bulk_wait_all() {
