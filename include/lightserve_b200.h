@@ -82,6 +82,26 @@ LSB_API int lsb_attn_fwd(const void* q, const void* k, const void* v, void* o, f
                  const int64_t* so, float scale, int causal, int dtype, int impl,
                  void* stream);
 
+/*
+ * Variable-length FlashAttention forward over sequences packed along the
+ * token axis (the prefill shape of a paged-KV server). lightserve's forward
+ * takes one [B, H, N, D] batch with Nq == Nkv (kernels/flash_attention.py:
+ * 192-199); its block manager admits prompts of different lengths
+ * (engine/request.py:86-93, engine/block_manager.py:47-157), which this
+ * entry point serves without padding. Sequence s holds tokens
+ * [cu_seqlens[s], cu_seqlens[s+1]) of q, k, v, o ([total_tokens, H, D],
+ * element strides {token, head, 1}); cu_seqlens is int32 [num_seqs + 1] in
+ * device memory, non-decreasing from 0 to total_tokens; max_seqlen bounds
+ * the longest sequence. Attention (causal within a sequence when causal != 0)
+ * never crosses sequences. lse (optional): fp32 [H, total_tokens].
+ * bf16 / fp16 with D in {64, 128} (tcgen05 kernel only).
+ */
+LSB_API int lsb_attn_fwd_varlen(const void* q, const void* k, const void* v, void* o, float* lse,
+                        const int32_t* cu_seqlens, int64_t num_seqs, int64_t max_seqlen,
+                        int64_t total_tokens, int64_t H, int64_t D,
+                        const int64_t* sq, const int64_t* sk, const int64_t* sv,
+                        const int64_t* so, float scale, int causal, int dtype, void* stream);
+
 /* Bytes of fp32 scratch lsb_attn_bwd needs: Dsum [B,H,N] + dQ accumulator
  * [B,H,N,D] (each region 256-byte aligned). */
 LSB_API int64_t lsb_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D);
@@ -167,6 +187,21 @@ LSB_API int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, int6
                               void* v_cache, int32_t* context_lens, int64_t S, int64_t H,
                               int64_t D, int64_t num_blocks, int64_t block_size, int dtype,
                               void* stream);
+
+/*
+ * Fused RoPE + paged KV-cache write for a packed prefill: lsb_rope_kv_write
+ * for T tokens of any sequences, each with its own position and cache slot
+ * (slot_mapping: int64 [T], block * block_size + offset as produced from
+ * engine/block_manager.py:58-61's tables; < 0 skips the cache write).
+ * Writes rotated q to q_out and (when k_out != NULL) rotated k to k_out,
+ * both [T, H, D] contiguous, for lsb_attn_fwd_varlen.
+ */
+LSB_API int lsb_rope_kv_write_slots(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                                    const void* cos_table, const void* sin_table, int64_t s_pos,
+                                    const int64_t* positions, const int64_t* slot_mapping,
+                                    void* q_out, void* k_out, void* k_cache, void* v_cache,
+                                    int64_t T, int64_t H, int64_t D, int64_t num_blocks,
+                                    int64_t block_size, int dtype, void* stream);
 
 /*
  * Fused SwiGLU of the Llama MLP: out = silu(gate) * up with

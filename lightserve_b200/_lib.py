@@ -46,6 +46,8 @@ SIGNATURES = {
     "lsb_rmsnorm_residual": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
     "lsb_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,
                           _F, _I, _I, _I, _P]),
+    "lsb_attn_fwd_varlen": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                 _I64P, _I64P, _I64P, _I64P, _F, _I, _I, _P]),
     "lsb_attn_bwd_workspace_size": (_I64, [_I64, _I64, _I64, _I64]),
     "lsb_attn_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                           _I64P, _I64P, _I64P, _I64P, _I64P, _I64P, _I64P, _I64P,
@@ -57,6 +59,8 @@ SIGNATURES = {
                               _I64, _I64, _I64, _I64, _F, _I, _P, _I64, _P]),
     "lsb_rope_kv_write": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P,
                                _I64, _I64, _I64, _I64, _I64, _I, _P]),
+    "lsb_rope_kv_write_slots": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
+                                     _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_swiglu": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_paged_decode_static_scratch_capacity": (_I64, []),
     "lsb_paged_decode_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,

@@ -79,6 +79,10 @@ struct Params {
   void* o;
   float* lse;
   int* work_counter;  // zeroed before launch; CTAs take work items from it
+  // Variable-length mode (non-NULL): sequences packed along the row axis,
+  // sequence s = rows [cu_seqlens[s], cu_seqlens[s+1]); "b" is then the
+  // sequence index, N the total row count, and LSE is [H, N].
+  const int* cu_seqlens;
   int64_t so_b, so_h, so_n;
   int H, N, BH;
   int num_q_ctas;
@@ -132,8 +136,12 @@ __device__ __forceinline__ float row_max(uint32_t (&sr)[4][32], int lim) {
 }
 
 // One work item: query rows [q0, q0 + 256) of one (batch, head) slice.
+// Rows are slice-relative; `base` is the slice's first row in the tensor
+// (its cu_seqlens entry in variable-length mode), `n` its length, `tb` the
+// batch coordinate of the TMA maps (0 in variable-length mode).
 struct Item {
   int bh, b, h, q0;
+  int base, n, tb;
   int nkv_t[TILES];  // K/V tiles each query tile visits (0: tile past the end)
   int nkv;
 };
@@ -149,11 +157,21 @@ __device__ __forceinline__ Item decode_item(int item, const Params& p) {
   w.h = w.bh % p.H;
   const int c = p.causal ? (nq - 1 - ci) : ci;  // causal: longest items first
   w.q0 = c * (TILES * BM);
-  const int nkv_all = (p.N + BN - 1) / BN;
+  if (p.cu_seqlens != nullptr) {
+    // Clamped to the tensor, so malformed offsets cannot reach outside it.
+    w.base = min(max(__ldg(p.cu_seqlens + w.b), 0), p.N);
+    w.n = min(max(__ldg(p.cu_seqlens + w.b + 1), w.base), p.N) - w.base;
+    w.tb = 0;
+  } else {
+    w.base = 0;
+    w.n = p.N;
+    w.tb = w.b;
+  }
+  const int nkv_all = (w.n + BN - 1) / BN;
 #pragma unroll
   for (int t = 0; t < TILES; ++t) {
     const int qt0 = w.q0 + t * BM;
-    w.nkv_t[t] = qt0 >= p.N ? 0 : (p.causal ? min(nkv_all, qt0 / BN + 1) : nkv_all);
+    w.nkv_t[t] = qt0 >= w.n ? 0 : (p.causal ? min(nkv_all, qt0 / BN + 1) : nkv_all);
   }
   w.nkv = max(w.nkv_t[0], w.nkv_t[1]);
   return w;
@@ -245,20 +263,26 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         const Item w = decode_item(item, p);
         for (int t = 0; t < TILES; ++t) {
           if (k > 0 && !mbar_wait(&q_empty[t], (k - 1) & 1, 0x103)) { ok = false; break; }
+          if (w.nkv_t[t] == 0) {  // tile past the slice end: nothing to load
+            mbar_arrive(&q_full[t]);
+            continue;
+          }
           mbar_arrive_expect_tx(&q_full[t], KC * CHUNK_BYTES);
           for (int kc = 0; kc < KC; ++kc)
             tma_load_4d(sQ + (t * KC + kc) * CHUNK_BYTES, &tq, &q_full[t], kc * 64,
-                        w.q0 + t * BM, w.h, w.b);
+                        w.base + w.q0 + t * BM, w.h, w.tb);
         }
         for (int j = 0; ok && j < w.nkv; ++j, ++J) {
           const int s = J % NS;
           if (J >= NS && !mbar_wait(&kv_empty[s], ((J / NS) - 1) & 1, 0x101)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[s], KC * CHUNK_BYTES);
           for (int kc = 0; kc < KC; ++kc)
-            tma_load_4d(sK + (s * KC + kc) * CHUNK_BYTES, &tk, &k_full[s], kc * 64, j * BN, w.h, w.b);
+            tma_load_4d(sK + (s * KC + kc) * CHUNK_BYTES, &tk, &k_full[s], kc * 64,
+                        w.base + j * BN, w.h, w.tb);
           mbar_arrive_expect_tx(&v_full[s], KC * CHUNK_BYTES);
           for (int kc = 0; kc < KC; ++kc)
-            tma_load_4d(sV + (s * KC + kc) * CHUNK_BYTES, &tv, &v_full[s], kc * 64, j * BN, w.h, w.b);
+            tma_load_4d(sV + (s * KC + kc) * CHUNK_BYTES, &tv, &v_full[s], kc * 64,
+                        w.base + j * BN, w.h, w.tb);
         }
       }
     }
@@ -361,9 +385,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         for (int i = 0; i < 4; ++i) tmem_ld32(lane_addr + t * 128 + 32 * i, sr[i]);
         tmem_ld_wait();
         const int kv0 = j * BN;
-        // Only the diagonal tile (causal) and the tile holding position N-1 need masks.
-        const bool need_mask = (kv0 + BN > p.N) || (p.causal && kv0 + BN - 1 > qt0);
-        const int lim = min(p.N, p.causal ? row_g + 1 : p.N) - kv0;  // valid columns < lim
+        // Only the diagonal tile (causal) and the tile holding the slice's last
+        // key need masks (in variable-length mode that tile's columns past
+        // the end hold the next sequence's keys).
+        const bool need_mask = (kv0 + BN > w.n) || (p.causal && kv0 + BN - 1 > qt0);
+        const int lim = min(w.n, p.causal ? row_g + 1 : w.n) - kv0;  // valid columns < lim
         const float mx = need_mask ? row_max<true>(sr, lim) : row_max<false>(sr, lim);
         const float m_new = fmaxf(m, mx * sl2);
         float alpha = 1.f;
@@ -425,7 +451,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tc_fence_after();
         const float inv_l = 1.0f / l;
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        2 * (w.b * p.so_b + w.h * p.so_h + (int64_t)row_g * p.so_n);
+                        2 * (w.tb * p.so_b + w.h * p.so_h + (int64_t)(w.base + row_g) * p.so_n);
         // Whole 32-byte sectors per store when aligned: with one row per
         // thread, 16-byte stores reach about half the SM's write bandwidth.
         const bool st32 = (reinterpret_cast<uintptr_t>(orow) & 31) == 0;
@@ -441,18 +467,21 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             const float a1 = __uint_as_float(ov[2 * cc + 1]) * inv_l;
             pk[cc] = FMT == 1 ? pack_bf16(a0, a1) : pack_f16(a0, a1);
           }
-          if (row_g < p.N && st32) {
+          if (row_g < w.n && st32) {
 #pragma unroll
             for (int v8 = 0; v8 < 2; ++v8) st_global_v8(orow + 64 * i + 32 * v8, &pk[8 * v8]);
-          } else if (row_g < p.N) {
+          } else if (row_g < w.n) {
             uint4* dst = reinterpret_cast<uint4*>(orow + 64 * i);
 #pragma unroll
             for (int v4 = 0; v4 < 4; ++v4)
               dst[v4] = make_uint4(pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2], pk[4 * v4 + 3]);
           }
         }
-        if (p.lse != nullptr && row_g < p.N)
-          p.lse[(int64_t)w.bh * p.N + row_g] = (m + __log2f(l)) * 0.6931471805599453f;
+        if (p.lse != nullptr && row_g < w.n) {
+          const int64_t li = p.cu_seqlens != nullptr ? (int64_t)w.h * p.N + w.base + row_g
+                                                     : (int64_t)w.bh * p.N + row_g;
+          p.lse[li] = (m + __log2f(l)) * 0.6931471805599453f;
+        }
         tc_fence_before();
       }
       jt += nkv_t;
@@ -484,11 +513,15 @@ bool attn_fwd_tc_eligible(const void* q, const void* k, const void* v, const voi
   return true;
 }
 
+// Dense mode: cu_seqlens == NULL, B slices of N rows. Variable-length mode:
+// B == 1, N = total rows, n_seqs sequences at cu_seqlens (device), the
+// longest max_seqlen rows.
 template <int D, int FMT>
 static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
                          int64_t B, int64_t H, int64_t N, const int64_t* sq, const int64_t* sk,
                          const int64_t* sv, const int64_t* so, float scale, int causal,
-                         int dtype, cudaStream_t st) {
+                         int dtype, cudaStream_t st, const int* cu_seqlens = nullptr,
+                         int64_t n_seqs = 0, int64_t max_seqlen = 0) {
   using namespace fa_fwd;
   CUtensorMap mq, mk, mv;
   int rc = make_bhnd_map(&mq, q, dtype, B, H, N, D, sq, 64, BM);
@@ -498,8 +531,11 @@ static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   Params p;
   p.o = o; p.lse = lse;
   p.so_b = so[0]; p.so_h = so[1]; p.so_n = so[2];
-  p.H = (int)H; p.N = (int)N; p.BH = (int)(B * H);
-  p.num_q_ctas = (int)((N + TILES * BM - 1) / (TILES * BM));
+  p.cu_seqlens = cu_seqlens;
+  p.H = (int)H; p.N = (int)N;
+  p.BH = (int)((cu_seqlens != nullptr ? n_seqs : B) * H);
+  const int64_t rows = cu_seqlens != nullptr ? max_seqlen : N;
+  p.num_q_ctas = (int)((rows + TILES * BM - 1) / (TILES * BM));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   // Work-item counter: a slot of g_work_counters per launch (rotating, so
@@ -522,7 +558,7 @@ static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
               "attn_fwd_tc smem attribute");
   // Persistent: one CTA per SM (shared memory and TMEM allow no more).
-  const int64_t n_items = B * H * p.num_q_ctas;
+  const int64_t n_items = (int64_t)p.BH * p.num_q_ctas;
   dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));
   kern<<<grid, THREADS, smem, st>>>(mq, mk, mv, p);
   LSB_CHECK_LAUNCH("attn_fwd_tc");
@@ -539,6 +575,26 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
               : launch_fa_fwd<128, 0>(q, k, v, o, lse, B, H, N, sq, sk, sv, so, scale, causal, dtype, st);
   return bf ? launch_fa_fwd<64, 1>(q, k, v, o, lse, B, H, N, sq, sk, sv, so, scale, causal, dtype, st)
             : launch_fa_fwd<64, 0>(q, k, v, o, lse, B, H, N, sq, sk, sv, so, scale, causal, dtype, st);
+}
+
+int attn_fwd_varlen_tc(const void* q, const void* k, const void* v, void* o, float* lse,
+                       const int* cu_seqlens, int64_t n_seqs, int64_t max_seqlen, int64_t T,
+                       int64_t H, int64_t D, const int64_t* sq, const int64_t* sk,
+                       const int64_t* sv, const int64_t* so, float scale, int causal, int dtype,
+                       cudaStream_t st) {
+  // [T, H, D] with strides {token, head, 1} as a [1, H, T, D] tensor.
+  const int64_t q4[4] = {0, sq[1], sq[0], 1}, k4[4] = {0, sk[1], sk[0], 1};
+  const int64_t v4[4] = {0, sv[1], sv[0], 1}, o4[4] = {0, so[1], so[0], 1};
+  const bool bf = dtype == LSB_DTYPE_BF16;
+  if (D == 128)
+    return bf ? launch_fa_fwd<128, 1>(q, k, v, o, lse, 1, H, T, q4, k4, v4, o4, scale, causal, dtype,
+                                      st, cu_seqlens, n_seqs, max_seqlen)
+              : launch_fa_fwd<128, 0>(q, k, v, o, lse, 1, H, T, q4, k4, v4, o4, scale, causal, dtype,
+                                      st, cu_seqlens, n_seqs, max_seqlen);
+  return bf ? launch_fa_fwd<64, 1>(q, k, v, o, lse, 1, H, T, q4, k4, v4, o4, scale, causal, dtype, st,
+                                   cu_seqlens, n_seqs, max_seqlen)
+            : launch_fa_fwd<64, 0>(q, k, v, o, lse, 1, H, T, q4, k4, v4, o4, scale, causal, dtype, st,
+                                   cu_seqlens, n_seqs, max_seqlen);
 }
 
 int attn_fwd_tc_device_error() {

@@ -33,6 +33,11 @@ int attn_fwd_tc(const void* q, const void* k, const void* v, void* o, float* lse
                 int64_t H, int64_t N, int64_t D, const int64_t* sq, const int64_t* sk,
                 const int64_t* sv, const int64_t* so, float scale, int causal, int dtype,
                 cudaStream_t st);
+int attn_fwd_varlen_tc(const void* q, const void* k, const void* v, void* o, float* lse,
+                       const int* cu_seqlens, int64_t n_seqs, int64_t max_seqlen, int64_t T,
+                       int64_t H, int64_t D, const int64_t* sq, const int64_t* sk,
+                       const int64_t* sv, const int64_t* so, float scale, int causal, int dtype,
+                       cudaStream_t st);
 // attn_bwd_sm100.cu
 bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const void* o,
                           const void* dout, const void* dq, const void* dk, const void* dv,
@@ -92,6 +97,34 @@ extern "C" int lsb_attn_fwd(const void* q, const void* k, const void* v, void* o
   }
   LSB_CHECK_ARG(impl == LSB_IMPL_AUTO || impl == LSB_IMPL_SIMT, "attn_fwd: bad impl %d", impl);
   return lsb::attn_fwd_simt(q, k, v, o, lse, B, H, N, D, sq, sk, sv, so, scale, causal, dtype, st);
+}
+
+extern "C" int lsb_attn_fwd_varlen(const void* q, const void* k, const void* v, void* o,
+                                   float* lse, const int32_t* cu_seqlens, int64_t num_seqs,
+                                   int64_t max_seqlen, int64_t total_tokens, int64_t H, int64_t D,
+                                   const int64_t* sq, const int64_t* sk, const int64_t* sv,
+                                   const int64_t* so, float scale, int causal, int dtype,
+                                   void* stream) {
+  int rc = check_attn_common("attn_fwd_varlen", num_seqs, H, total_tokens, D, dtype);
+  if (rc) return rc;
+  LSB_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= total_tokens,
+                "attn_fwd_varlen: max_seqlen %lld outside [0, total_tokens=%lld]",
+                (long long)max_seqlen, (long long)total_tokens);
+  if (num_seqs == 0 || H == 0 || total_tokens == 0 || max_seqlen == 0) return LSB_OK;
+  LSB_CHECK_ARG(q && k && v && o && cu_seqlens && sq && sk && sv && so,
+                "attn_fwd_varlen: null pointer");
+  // The packed [T, H, D] tensors are checked as [1, H, T, D] with strides
+  // {0, head, token, 1}.
+  const int64_t q4[4] = {0, sq[1], sq[0], 1}, k4[4] = {0, sk[1], sk[0], 1};
+  const int64_t v4[4] = {0, sv[1], sv[0], 1}, o4[4] = {0, so[1], so[0], 1};
+  LSB_CHECK_ARG(sq[2] == 1 && sk[2] == 1 && sv[2] == 1 && so[2] == 1 &&
+                    lsb::attn_fwd_tc_eligible(q, k, v, o, 1, H, total_tokens, D, q4, k4, v4, o4,
+                                              dtype),
+                "attn_fwd_varlen: needs bf16/fp16, D in {64,128}, unit d-stride and 16-byte "
+                "aligned token / head strides");
+  return lsb::attn_fwd_varlen_tc(q, k, v, o, lse, cu_seqlens, num_seqs, max_seqlen, total_tokens,
+                                 H, D, sq, sk, sv, so, scale, causal, dtype,
+                                 (cudaStream_t)stream);
 }
 
 extern "C" int64_t lsb_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t N, int64_t D) {

@@ -705,7 +705,89 @@ __global__ void rope_kv_write_kernel(const T* __restrict__ qkv, int64_t s_s, int
   }
 }
 
+// Packed-prefill variant: one CTA per token of a [T, 3, H, D] QKV buffer,
+// the token's cache slot given directly (slot_mapping, block * block_size +
+// offset, < 0: no cache write, as in lsb_kv_cache_write). Rotated q and k
+// also go to packed [T, H, D] outputs for the variable-length attention.
+template <typename T>
+__global__ void rope_kv_write_slots_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part,
+                                           int64_t s_h, const T* __restrict__ cos_t,
+                                           const T* __restrict__ sin_t, int64_t s_pos,
+                                           const int64_t* __restrict__ positions,
+                                           const int64_t* __restrict__ slot_mapping,
+                                           T* __restrict__ q_out, T* __restrict__ k_out,
+                                           T* __restrict__ k_cache, T* __restrict__ v_cache,
+                                           int H, int D, int64_t num_slots, int bs) {
+  const int64_t t = blockIdx.x;
+  const int64_t pos = positions[t];
+  const int64_t slot = slot_mapping[t];
+  const bool write = slot >= 0 && slot < num_slots;
+  const int64_t blk = slot / bs, off = slot % bs;
+  const int half = D / 2;
+  const T* cs = cos_t + pos * s_pos;
+  const T* sn = sin_t + pos * s_pos;
+  const T* row = qkv + t * s_s;
+  for (int idx = threadIdx.x; idx < H * half; idx += blockDim.x) {
+    const int h = idx / half, i = idx % half;
+    const float c0 = to_f(cs[i]), c1 = to_f(cs[i + half]);
+    const float n0 = to_f(sn[i]), n1 = to_f(sn[i + half]);
+    // rotate_half(x) = [-x2, x1]; every product and sum rounded to T.
+    auto rope = [&](float x1, float x2, T& o1, T& o2) {
+      const float a = to_f(from_f<T>(__fmul_rn(x1, c0)));
+      const float b = to_f(from_f<T>(__fmul_rn(-x2, n0)));
+      o1 = from_f<T>(__fadd_rn(a, b));
+      const float c = to_f(from_f<T>(__fmul_rn(x2, c1)));
+      const float d = to_f(from_f<T>(__fmul_rn(x1, n1)));
+      o2 = from_f<T>(__fadd_rn(c, d));
+    };
+    const T* qh = row + h * s_h;
+    const T* kh = row + s_part + h * s_h;
+    const T* vh = row + 2 * s_part + h * s_h;
+    const int64_t o = (t * H + h) * D;
+    T q1, q2, k1, k2;
+    rope(to_f(qh[i]), to_f(qh[i + half]), q1, q2);
+    rope(to_f(kh[i]), to_f(kh[i + half]), k1, k2);
+    q_out[o + i] = q1;
+    q_out[o + i + half] = q2;
+    if (k_out != nullptr) {
+      k_out[o + i] = k1;
+      k_out[o + i + half] = k2;
+    }
+    if (write) {
+      const int64_t dst = ((blk * H + h) * bs + off) * D;
+      k_cache[dst + i] = k1;
+      k_cache[dst + i + half] = k2;
+      v_cache[dst + i] = vh[i];
+      v_cache[dst + i + half] = vh[i + half];
+    }
+  }
+}
+
 }  // namespace lsb
+
+extern "C" int lsb_rope_kv_write_slots(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                                       const void* cos_table, const void* sin_table, int64_t s_pos,
+                                       const int64_t* positions, const int64_t* slot_mapping,
+                                       void* q_out, void* k_out, void* k_cache, void* v_cache,
+                                       int64_t T, int64_t H, int64_t D, int64_t num_blocks,
+                                       int64_t block_size, int dtype, void* stream) {
+  LSB_CHECK_ARG(T >= 0 && H > 0 && D > 0 && (D % 2) == 0 && num_blocks > 0 && block_size > 0,
+                "rope_kv_write_slots: bad sizes");
+  if (T == 0) return LSB_OK;
+  LSB_CHECK_ARG(qkv && cos_table && sin_table && positions && slot_mapping && q_out && k_cache &&
+                    v_cache,
+                "rope_kv_write_slots: null pointer");
+  LSB_CHECK_ARG(T <= 0x7fffffff, "rope_kv_write_slots: T too large");
+  cudaStream_t st = (cudaStream_t)stream;
+  return LSB_DISPATCH_DTYPE(dtype, Tp, [&] {
+    lsb::rope_kv_write_slots_kernel<Tp><<<(unsigned)T, 256, 0, st>>>(
+        (const Tp*)qkv, s_s, s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos,
+        positions, slot_mapping, (Tp*)q_out, (Tp*)k_out, (Tp*)k_cache, (Tp*)v_cache, (int)H,
+        (int)D, num_blocks * block_size, (int)block_size);
+    LSB_CHECK_LAUNCH("rope_kv_write_slots");
+    return LSB_OK;
+  });
+}
 
 extern "C" int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
                                  const void* cos_table, const void* sin_table, int64_t s_pos,

@@ -14,6 +14,7 @@ head dims run the CUDA-core kernel of the same library.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -54,6 +55,57 @@ def flash_attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     o = torch.empty_like(q)
     _attn_fwd(q, k, v, o, None, causal)
     return o
+
+
+def flash_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           cu_seqlens: torch.Tensor, max_seqlen: int, causal: bool = False,
+                           out: torch.Tensor | None = None,
+                           lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention over sequences packed along the token axis.
+
+    q, k, v: ``[T, H, D]`` (bf16/fp16, D in {64, 128}, unit last stride, any
+    16-byte aligned token/head strides, e.g. views into a fused QKV
+    projection); ``cu_seqlens``: int32 ``[num_seqs + 1]`` on the same device,
+    sequence s = tokens ``[cu_seqlens[s], cu_seqlens[s+1])``; ``max_seqlen``:
+    an upper bound on the longest sequence. Each sequence attends only to
+    itself (causally when ``causal``) with scale ``1/sqrt(D)``, as
+    ``flash_attention_forward`` on that sequence alone would. Returns ``out``
+    (default ``empty_like(q)``); ``lse`` (optional, fp32 ``[H, T]``) receives
+    the per-row log-sum-exp. lightserve's forward has no variable-length form
+    (``kernels/flash_attention.py:192-199`` requires one N for the batch);
+    this is the packed prefill a paged-KV server needs for prompts of
+    different lengths (``engine/request.py:86-93``)."""
+    assert q.ndim == 3 and k.ndim == 3 and v.ndim == 3, "expected q/k/v as [T, H, D]"
+    assert q.shape == k.shape == v.shape, (
+        f"q/k/v shapes must match, got {tuple(q.shape)}/{tuple(k.shape)}/{tuple(v.shape)}"
+    )
+    assert q.is_cuda and k.is_cuda and v.is_cuda, "lightserve_b200 kernels need CUDA tensors"
+    assert q.dtype == k.dtype == v.dtype, f"dtype mismatch: q={q.dtype} k={k.dtype} v={v.dtype}"
+    assert q.dtype in (torch.bfloat16, torch.float16), "varlen attention needs bf16 or fp16"
+    assert q.device == k.device == v.device == cu_seqlens.device, "tensors must be on one device"
+    assert cu_seqlens.ndim == 1 and cu_seqlens.dtype == torch.int32 and cu_seqlens.is_contiguous(), (
+        "cu_seqlens must be a contiguous int32 vector [num_seqs + 1]"
+    )
+    assert cu_seqlens.numel() >= 1, "cu_seqlens needs at least one entry"
+    T, H, D = q.shape
+    assert D in (64, 128), f"varlen attention supports D in {{64, 128}}, got {D}"
+    assert 0 <= int(max_seqlen) <= T, f"max_seqlen {max_seqlen} outside [0, {T}]"
+    if out is None:
+        out = torch.empty_like(q)
+    assert out.shape == q.shape and out.dtype == q.dtype and out.device == q.device
+    if lse is not None:
+        assert lse.shape == (H, T) and lse.dtype == torch.float32 and lse.is_contiguous()
+    lib = _lib.load()
+    s3 = lambda t: (ctypes.c_int64 * 3)(*t.stride())  # noqa: E731
+    with _lib.device_guard(q.device):
+        rc = lib.lsb_attn_fwd_varlen(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _lib.ptr(lse),
+            cu_seqlens.data_ptr(), cu_seqlens.numel() - 1, int(max_seqlen), T, H, D,
+            s3(q), s3(k), s3(v), s3(out), 1.0 / math.sqrt(D), int(bool(causal)),
+            _lib.dtype_code(q.dtype), _lib.stream_ptr(q.device),
+        )
+    _lib.check(rc, "lsb_attn_fwd_varlen")
+    return out
 
 
 def flash_attention_forward_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,

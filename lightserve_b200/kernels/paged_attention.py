@@ -133,3 +133,38 @@ def rope_kv_write(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, posit
         )
     _lib.check(rc, "lsb_rope_kv_write")
     return q_out
+
+
+def rope_kv_write_slots(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                        positions: torch.Tensor, slot_mapping: torch.Tensor, q_out: torch.Tensor,
+                        k_out: torch.Tensor | None, k_cache: torch.Tensor,
+                        v_cache: torch.Tensor) -> torch.Tensor:
+    """Packed-prefill RoPE + KV-cache write: ``rope_kv_write`` for T tokens of any
+    sequences, each with its own position (int64 [T]) and cache slot
+    (``slot_mapping`` int64 [T], ``block * block_size + offset``; < 0 skips the
+    write). Rotated q goes to ``q_out`` and rotated k to ``k_out`` (both
+    [T, H, D] contiguous; ``k_out`` optional), as inputs of
+    ``flash_attention_varlen``. Same rounding as ``rope_kv_write``."""
+    assert qkv.ndim == 4 and qkv.shape[1] == 3 and qkv.stride(3) == 1, "qkv must be [T, 3, H, D]"
+    T, _, H, D = qkv.shape
+    assert k_cache.ndim == 4 and k_cache.shape == v_cache.shape and k_cache.is_contiguous()
+    assert v_cache.is_contiguous()
+    nb, Hc, bs, Dc = k_cache.shape
+    assert (Hc, Dc) == (H, D)
+    assert cos.shape == sin.shape and cos.shape[1] == D and cos.stride() == sin.stride() and cos.stride(1) == 1
+    assert qkv.dtype == cos.dtype == sin.dtype == k_cache.dtype == v_cache.dtype == q_out.dtype
+    assert q_out.shape == (T, H, D) and q_out.is_contiguous()
+    if k_out is not None:
+        assert k_out.shape == (T, H, D) and k_out.is_contiguous() and k_out.dtype == q_out.dtype
+    assert positions.dtype == torch.int64 and positions.shape == (T,) and positions.is_contiguous()
+    assert slot_mapping.dtype == torch.int64 and slot_mapping.shape == (T,) and slot_mapping.is_contiguous()
+    lib = _lib.load()
+    with _lib.device_guard(qkv.device):
+        rc = lib.lsb_rope_kv_write_slots(
+            qkv.data_ptr(), qkv.stride(0), qkv.stride(1), qkv.stride(2), cos.data_ptr(), sin.data_ptr(),
+            cos.stride(0), positions.data_ptr(), slot_mapping.data_ptr(), q_out.data_ptr(),
+            _lib.ptr(k_out), k_cache.data_ptr(), v_cache.data_ptr(), T, H, D, nb, bs,
+            _lib.dtype_code(qkv.dtype), _lib.stream_ptr(qkv.device),
+        )
+    _lib.check(rc, "lsb_rope_kv_write_slots")
+    return q_out

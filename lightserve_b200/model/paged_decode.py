@@ -16,6 +16,13 @@ the cache slot from the block table, context lengths) ->
 ``paged_decode_attention`` (lsb kernel) -> O projection -> add+RMSNorm ->
 SwiGLU MLP. All buffers are static, so a step is graph-capturable.
 
+Prefill: with a bf16/fp16 model and head_dim 64 or 128, every admitted prompt
+runs in ONE packed forward ([sum of prompt lengths, hidden]: the GEMMs see
+all prompt tokens at once, ``rope_kv_write_slots`` rotates q/k and fills the
+cache through each token's slot, ``flash_attention_varlen`` attends within
+each prompt); other models prefill one request at a time through
+``llama_forward``.
+
 Block reservation: at admission the runner asks the block manager for every
 block the request will need over ``max_new_tokens`` (``allocate`` for the
 prompt, then the same ``append_slot`` sequence the scheduler would issue one
@@ -31,8 +38,9 @@ import torch.nn.functional as F
 from ..engine import BlockManager, Request
 from ..kernels.fused_rmsnorm_residual import fused_add_rmsnorm
 from ..kernels.fused_swiglu import silu_and_mul
+from ..kernels.flash_attention import flash_attention_varlen
 from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
-                                        rope_kv_write, write_kv_cache)
+                                        rope_kv_write, rope_kv_write_slots, write_kv_cache)
 from .minimal_llama import LlamaConfig, LlamaWeights, llama_forward, precompute_rope
 
 
@@ -91,12 +99,20 @@ class PagedDecoder:
         self.requests: list = []
 
     # ------------------------------------------------------------ admission --
-    def admit(self, requests, max_new_tokens: int) -> torch.Tensor:
-        """Allocates blocks, runs each prompt's prefill into the cache and returns
-        the first greedy token of every request (int64 [len(requests)])."""
+    def packed_prefill_supported(self) -> bool:
+        return self.cfg.dtype in (torch.bfloat16, torch.float16) and self.cfg.head_dim in (64, 128)
+
+    def admit(self, requests, max_new_tokens: int, packed: bool | None = None) -> torch.Tensor:
+        """Allocates blocks, runs the prompts' prefill into the cache and returns
+        the first greedy token of every request (int64 [len(requests)]).
+        ``packed`` (default: when supported) prefills all prompts in one packed
+        forward instead of one ``llama_forward`` per request."""
         assert len(requests) <= self.S
         bs = self.cache.block_size
+        if packed is None:
+            packed = self.packed_prefill_supported()
         first = []
+        tables = []
         for r in requests:
             assert self.bm.can_allocate(r), f"not enough KV blocks for {r.request_id}"
             self.bm.allocate(r)
@@ -108,6 +124,9 @@ class PagedDecoder:
             del r.output_token_ids[n0:]
             table = self.bm.get_block_table(r)
             assert len(table) <= self.MB, "max_blocks_per_seq too small"
+            tables.append(table)
+            if packed:
+                continue
             ids = torch.tensor([r.prompt_token_ids], dtype=torch.int64, device=self.device)
             n = ids.shape[1]
             slots = slots_for_positions(table, range(n), bs).to(self.device)
@@ -118,6 +137,8 @@ class PagedDecoder:
 
             logits = llama_forward(self.w, self.cfg, ids, causal=True, kv_sink=sink, last_only=True)
             first.append(logits[0, -1].argmax(-1))
+        if packed:
+            first = list(self.prefill_packed(requests, tables)) if requests else []
         self.requests = list(requests)
         nreq = len(requests)
         bt = self.bm.as_tensor(requests, self.MB)
@@ -130,6 +151,42 @@ class PagedDecoder:
         self.positions[:nreq].copy_(torch.tensor([len(r.prompt_token_ids) for r in requests],
                                                  dtype=torch.int64, device=self.device))
         return first_t
+
+    def prefill_packed(self, requests, tables) -> torch.Tensor:
+        """One forward over every prompt token of ``requests`` (packed along the
+        token axis), writing each token's K/V into its cache slot; returns the
+        greedy next token of each request (int64 [len(requests)])."""
+        assert self.packed_prefill_supported()
+        cfg, bs, dev = self.cfg, self.cache.block_size, self.device
+        H, D, Hd = cfg.n_heads, cfg.head_dim, cfg.hidden_size
+        lens = [len(r.prompt_token_ids) for r in requests]
+        assert min(lens) > 0, "empty prompt"
+        T = sum(lens)
+        ids = torch.tensor([t for r in requests for t in r.prompt_token_ids], dtype=torch.int64)
+        positions = torch.cat([torch.arange(n, dtype=torch.int64) for n in lens])
+        slots = torch.cat([slots_for_positions(tb, range(n), bs) for tb, n in zip(tables, lens)])
+        cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
+        ids, positions, slots, cu = (t.to(dev, non_blocking=True) for t in (ids, positions, slots, cu))
+        residual = F.embedding(ids, self.w.embed_tokens)
+        x = torch.zeros_like(residual)
+        q_rot = torch.empty(T, H, D, dtype=cfg.dtype, device=dev)
+        k_rot = torch.empty_like(q_rot)
+        attn = torch.empty_like(q_rot)
+        for li, layer in enumerate(self.w.layers):
+            fz = self.fused[li]
+            normed, residual = fused_add_rmsnorm(x, residual, layer.input_layernorm_weight, eps=cfg.rms_eps)
+            qkv = (normed @ fz.w_qkv).view(T, 3, H, D)
+            rope_kv_write_slots(qkv, self.cos, self.sin, positions, slots, q_rot, k_rot,
+                                self.cache.k[li], self.cache.v[li])
+            flash_attention_varlen(q_rot, k_rot, qkv[:, 2], cu, max(lens), causal=True, out=attn)
+            x = attn.view(T, Hd) @ layer.o_proj
+            normed2, residual = fused_add_rmsnorm(x, residual, layer.post_attention_layernorm_weight,
+                                                  eps=cfg.rms_eps)
+            x = silu_and_mul(normed2 @ fz.w_gu) @ layer.down_proj
+        last = (cu[1:] - 1).long()
+        final, _ = fused_add_rmsnorm(x[last].contiguous(), residual[last].contiguous(), self.w.norm_weight,
+                                     eps=cfg.rms_eps)
+        return (final @ self.w.lm_head).argmax(-1)
 
     # ----------------------------------------------------------------- step --
     def step(self) -> torch.Tensor:

@@ -76,3 +76,23 @@ def test_forward_host_rejects_device_tensors():
     q = torch.zeros(1, 1, 4, 8, device="meta")
     with pytest.raises(AssertionError):
         flash_attention_forward_host(q, q, q)
+
+
+def test_varlen_rejects_bad_input():
+    from lightserve_b200.kernels import flash_attention_varlen
+    cu = torch.tensor([0, 16], dtype=torch.int32)
+    with pytest.raises(AssertionError):  # [B, H, N, D] instead of packed [T, H, D]
+        flash_attention_varlen(*(torch.randn(1, 2, 16, 64) for _ in range(3)), cu, 16)
+    with pytest.raises(AssertionError):  # shape mismatch
+        flash_attention_varlen(torch.randn(16, 2, 64), torch.randn(16, 2, 64), torch.randn(8, 2, 64), cu, 16)
+    with pytest.raises(AssertionError):  # CPU tensors
+        flash_attention_varlen(*(torch.randn(16, 2, 64, dtype=torch.bfloat16) for _ in range(3)), cu, 16)
+
+
+def test_rope_kv_write_slots_rejects_bad_input():
+    from lightserve_b200.kernels import rope_kv_write_slots
+    qkv = torch.randn(4, 3, 2, 8)
+    cache = torch.zeros(4, 2, 16, 8)
+    with pytest.raises(AssertionError):  # slot mapping must be int64
+        rope_kv_write_slots(qkv, torch.ones(8, 8), torch.ones(8, 8), torch.arange(4),
+                            torch.arange(4, dtype=torch.int32), torch.empty(4, 2, 8), None, cache, cache.clone())
