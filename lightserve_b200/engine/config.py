@@ -1,5 +1,6 @@
 """KV-cache sizing config, same fields and checks as lightserve's
-``engine/config.py:16-43`` ``CacheConfig`` (block_size defaults to 16, ``:34``).
+``engine/config.py:16-43`` ``CacheConfig`` (block_size defaults to 16, ``:34``),
+and the scheduler limits of ``engine/config.py:46-68`` ``SchedulerConfig``.
 
 ``kv_cache_bytes_per_block`` adds the physical-size arithmetic the reference
 leaves to the deployment (``engine/config.py:7-11``): a block stores K and V for
@@ -22,6 +23,19 @@ class CacheConfig:
         assert 0 <= self.watermark_blocks <= self.num_gpu_blocks, (
             "watermark_blocks must fit within num_gpu_blocks"
         )
+
+
+@dataclass(frozen=True)
+class SchedulerConfig:
+    """max_num_seqs: most requests RUNNING at once (the decode batch);
+    max_num_batched_tokens: tokens one schedule() call may hand to the model
+    (whole prompts of admitted requests plus one per decoding request)."""
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 2048
+
+    def __post_init__(self):
+        assert self.max_num_seqs > 0, "max_num_seqs must be positive"
+        assert self.max_num_batched_tokens > 0, "max_num_batched_tokens must be positive"
 
 
 def kv_cache_bytes_per_block(block_size: int, n_layers: int, n_heads: int, head_dim: int,

@@ -125,18 +125,8 @@ class PagedDecoder:
             table = self.bm.get_block_table(r)
             assert len(table) <= self.MB, "max_blocks_per_seq too small"
             tables.append(table)
-            if packed:
-                continue
-            ids = torch.tensor([r.prompt_token_ids], dtype=torch.int64, device=self.device)
-            n = ids.shape[1]
-            slots = slots_for_positions(table, range(n), bs).to(self.device)
-
-            def sink(li, k, v):
-                write_kv_cache(k[0].transpose(0, 1), v[0].transpose(0, 1), self.cache.k[li],
-                               self.cache.v[li], slots)
-
-            logits = llama_forward(self.w, self.cfg, ids, causal=True, kv_sink=sink, last_only=True)
-            first.append(logits[0, -1].argmax(-1))
+            if not packed:
+                first.append(self._prefill_one(r.prompt_token_ids, table))
         if packed:
             first = list(self.prefill_packed(requests, tables)) if requests else []
         self.requests = list(requests)
@@ -152,17 +142,45 @@ class PagedDecoder:
                                                  dtype=torch.int64, device=self.device))
         return first_t
 
+    def _prefill_one(self, token_ids, table) -> torch.Tensor:
+        """One sequence through ``llama_forward`` with its K/V sent to the cache
+        slots of ``table``; returns its greedy next token (0-d int64)."""
+        ids = torch.tensor([list(token_ids)], dtype=torch.int64, device=self.device)
+        slots = slots_for_positions(table, range(ids.shape[1]), self.cache.block_size).to(self.device)
+
+        def sink(li, k, v):
+            write_kv_cache(k[0].transpose(0, 1), v[0].transpose(0, 1), self.cache.k[li],
+                           self.cache.v[li], slots)
+
+        logits = llama_forward(self.w, self.cfg, ids, causal=True, kv_sink=sink, last_only=True)
+        return logits[0, -1].argmax(-1)
+
+    def prefill(self, token_lists, tables) -> list:
+        """Prefill of whole sequences (prompt plus any tokens generated before a
+        preemption) into the cache slots of ``tables``; returns each one's greedy
+        next token (host ints). Packed when supported, else one at a time."""
+        if not token_lists:
+            return []
+        if self.packed_prefill_supported():
+            return self.prefill_sequences(token_lists, tables).tolist()
+        return [int(self._prefill_one(t, tb)) for t, tb in zip(token_lists, tables)]
+
     def prefill_packed(self, requests, tables) -> torch.Tensor:
-        """One forward over every prompt token of ``requests`` (packed along the
+        """``prefill_sequences`` over the prompts of ``requests``."""
+        return self.prefill_sequences([r.prompt_token_ids for r in requests], tables)
+
+    def prefill_sequences(self, token_lists, tables) -> torch.Tensor:
+        """One forward over every token of ``token_lists`` (packed along the
         token axis), writing each token's K/V into its cache slot; returns the
-        greedy next token of each request (int64 [len(requests)])."""
+        greedy next token of each sequence (int64 [len(token_lists)])."""
         assert self.packed_prefill_supported()
         cfg, bs, dev = self.cfg, self.cache.block_size, self.device
         H, D, Hd = cfg.n_heads, cfg.head_dim, cfg.hidden_size
-        lens = [len(r.prompt_token_ids) for r in requests]
+        lens = [len(t) for t in token_lists]
         assert min(lens) > 0, "empty prompt"
+        assert max(lens) <= cfg.max_seq_len, "sequence longer than the RoPE table"
         T = sum(lens)
-        ids = torch.tensor([t for r in requests for t in r.prompt_token_ids], dtype=torch.int64)
+        ids = torch.tensor([t for seq in token_lists for t in seq], dtype=torch.int64)
         positions = torch.cat([torch.arange(n, dtype=torch.int64) for n in lens])
         slots = torch.cat([slots_for_positions(tb, range(n), bs) for tb, n in zip(tables, lens)])
         cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
@@ -187,6 +205,34 @@ class PagedDecoder:
         final, _ = fused_add_rmsnorm(x[last].contiguous(), residual[last].contiguous(), self.w.norm_weight,
                                      eps=cfg.rms_eps)
         return (final @ self.w.lm_head).argmax(-1)
+
+    # ------------------------------------------------------- slot decode --
+    def decode_slots(self, slots, tokens, positions, tables, use_graph: bool = True) -> list:
+        """One decode step for the sequences in batch rows ``slots``: row
+        slots[i] processes tokens[i] at positions[i] with block table
+        tables[i]; every other row is idle (no block table, so no cache write).
+        Returns the greedy next token of each given slot (host ints). The
+        CUDA graph is captured on first use, with every row idle."""
+        if use_graph and self.graph is None:
+            self.block_tables.fill_(-1)
+            self.capture()
+        tok = torch.zeros(self.S, dtype=torch.int64)
+        pos = torch.zeros(self.S, dtype=torch.int64)
+        bt = torch.full((self.S, self.MB), -1, dtype=torch.int32)
+        for s_, t, p_, tb in zip(slots, tokens, positions, tables):
+            assert len(tb) <= self.MB, "block table longer than max_blocks_per_seq"
+            assert p_ < self.cfg.max_seq_len, "position beyond the RoPE table"
+            tok[s_], pos[s_] = t, p_
+            bt[s_, :len(tb)] = torch.tensor(tb, dtype=torch.int32)
+        self.tokens.copy_(tok, non_blocking=True)
+        self.positions.copy_(pos, non_blocking=True)
+        self.block_tables.copy_(bt, non_blocking=True)
+        if use_graph:
+            self.graph.replay()
+        else:
+            self.step()
+        nxt = self.tokens.cpu()
+        return [int(nxt[s_]) for s_ in slots]
 
     # ----------------------------------------------------------------- step --
     def step(self) -> torch.Tensor:
