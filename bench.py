@@ -15,6 +15,7 @@ collective on the data path ("scaling": "weak"); times are the max over ranks.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -36,6 +37,22 @@ DEC_CFG = dict(S=64, steps=128, ctx_lo=512, ctx_hi=4096, block_size=16)
 
 
 # ----------------------------------------------------------------- plumbing --
+@contextlib.contextmanager
+def _stdout_to_stderr():
+    """Sends file-descriptor-level stdout to stderr (NCCL prints its version
+    banner on stdout when the communicator comes up; stdout carries only the
+    JSON line)."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -44,7 +61,9 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        with _stdout_to_stderr():
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier()
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return rank, ws, local
