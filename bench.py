@@ -257,6 +257,28 @@ def bench_rmsnorm(steps, warmup, ws, rank):
             "kernel_ms": statistics.mean(per), "launches_per_step": 1}
 
 
+def bench_varlen(steps, warmup, ws, rank):
+    """Packed (variable-length) causal attention over config 5's prompt set:
+    64 sequences with lengths U[512, 4096], 16 heads x 128, bf16 -- one
+    layer's prefill attention."""
+    from lightserve_b200.kernels import flash_attention_varlen
+
+    c = DEC_CFG
+    g = torch.Generator().manual_seed(rank)
+    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
+    T, H, D = sum(lens), 16, 128
+    gen = torch.Generator(device="cuda").manual_seed(2000 + rank)
+    q, k, v = (_randn((T, H, D), torch.bfloat16, gen) for _ in range(3))
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    total_ms, _ = time_cuda(lambda: flash_attention_varlen(q, k, v, cu, max(lens), causal=True, out=out),
+                            steps, warmup, ws)
+    ms = total_ms / steps
+    flops = sum(attn_fwd_flops(1, H, n, D, True) for n in lens)
+    return {"ms": ms, "flops": flops, "tokens": T, "value": ws * flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "launches_per_step": 1}
+
+
 def bench_decode(steps, warmup, ws, rank):
     from lightserve_b200.engine import BlockManager, Request
     from lightserve_b200.model.minimal_llama import decode_bench_config, init_weights
@@ -397,7 +419,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--only", default="fwd,bwd,rmsnorm,decode,context",
+    ap.add_argument("--only", default="fwd,bwd,rmsnorm,varlen,decode,context",
                     help="comma list of workloads (fwd is always run: it is the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--strong", action="store_true",
@@ -421,6 +443,10 @@ def main():
     if "rmsnorm" in only:
         secondary["rmsnorm"] = bench_rmsnorm(args.steps, args.warmup, ws, rank)
         secondary["rmsnorm"]["frac_of_peak"] = secondary["rmsnorm"]["value"] / ws / peaks["hbm_gbs"]
+    if "varlen" in only:
+        secondary["varlen_prefill_attn"] = bench_varlen(args.steps, args.warmup, ws, rank)
+        secondary["varlen_prefill_attn"]["frac_of_peak"] = (secondary["varlen_prefill_attn"]["value"] / ws
+                                                             / peaks["bf16_tflops"])
     if "decode" in only:
         secondary["paged_decode"] = bench_decode(min(args.steps * 4, 128), args.warmup, ws, rank)
     if ws == 1 and "context" in only:
