@@ -20,7 +20,9 @@
 //  * warpgroups 1 and 2: softmax for query tile 0 and 1, one thread per row
 //    (TMEM lane). Each thread loads its 128 scores with tcgen05.ld, takes the
 //    row max, exponentiates with ex2 on log2(e)-prescaled scores, writes P as
-//    packed 16-bit pairs over the first 64 columns of its S buffer, and
+//    packed 16-bit pairs over the first 64 columns of its S buffer in two
+//    halves (keys [0,64) then [64,128), each with its own p_full barrier, so
+//    the first half's PV MMAs overlap the second half's exponentials), and
 //    rescales O in TMEM only when the running max grew by more than 2^8
 //    (otherwise the stale max is kept; values stay within fp32/bf16 range).
 //    At the end of an item the warpgroup normalises and stores its O rows
@@ -67,8 +69,8 @@ struct Smem {
   static constexpr int V_OFF = K_OFF + NS * KC * CHUNK_BYTES;
   static constexpr int BAR_OFF = V_OFF + NS * KC * CHUNK_BYTES;
   // barriers: q_full[2], q_empty[2], k_full[NS], v_full[NS], kv_empty[NS], s_full[2],
-  // p_full[2], pv_done[2], item_full[NIS], item_empty[NIS]
-  static constexpr int NBAR = 2 * TILES + 3 * NS + 3 * TILES + 2 * NIS;
+  // p_full[2][2], pv_done[2], item_full[NIS], item_empty[NIS]
+  static constexpr int NBAR = 2 * TILES + 3 * NS + 4 * TILES + 2 * NIS;
   static constexpr int TMEM_SLOT_OFF = BAR_OFF + NBAR * 8;
   static constexpr int ITEM_OFF = TMEM_SLOT_OFF + 16;
   static constexpr int BYTES = ITEM_OFF + NIS * 4;
@@ -192,8 +194,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint64_t* v_full = k_full + NS;              // [NS]
   uint64_t* kv_empty = v_full + NS;            // [NS]
   uint64_t* s_full = kv_empty + NS;            // [TILES]
-  uint64_t* p_full = s_full + TILES;           // [TILES]
-  uint64_t* pv_done = p_full + TILES;          // [TILES]
+  // [TILES][2]: the P of keys [0, 64) / [64, 128) of the step is in TMEM
+  // (the first half's PV MMAs run while the softmax computes the second).
+  uint64_t* p_full = s_full + TILES;
+  uint64_t* pv_done = p_full + 2 * TILES;      // [TILES]
   uint64_t* item_full = pv_done + TILES;       // [NIS]
   uint64_t* item_empty = item_full + NIS;      // [NIS]: 9 arrivals (MMA, 8 softmax warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT_OFF);
@@ -216,7 +220,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       mbar_init(&q_full[t], 1);
       mbar_init(&q_empty[t], 1);
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], BM);
+      mbar_init(&p_full[2 * t], BM);
+      mbar_init(&p_full[2 * t + 1], BM);
       mbar_init(&pv_done[t], 1);
     }
     for (int s = 0; s < NS; ++s) {
@@ -305,16 +310,19 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
         mma_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int J, bool acc) {
+      // PV over keys [64 h, 64 h + 64) of the K/V tile (K-steps 4h .. 4h+3);
+      // the second half commits pv_done.
+      auto issue_pv_half = [&](int t, int J, bool acc, int h) {
         const int s = J % NS;
         const uint32_t d_tmem = tmem + 256 + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int k4 = 0; k4 < BN / 32; ++k4) {
+          const int kk = h * (BN / 32) + k4;
           const uint64_t bd =
               smem_desc_sw128(v_base + (s * KC) * CHUNK_BYTES + kk * 2048, CHUNK_BYTES, 1024);
           mma_ts(d_tmem, tmem + t * 128 + kk * 8, bd, IDESC_PV, (acc || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&pv_done[t]);
+        if (h == 1) mma_commit(&pv_done[t]);
       };
       int J = 0;                     // running K/V tile count
       int jt[TILES] = {0, 0};        // running K/V step count per query tile
@@ -337,11 +345,14 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           if (!mbar_wait(&v_full[s], ((J + j) / NS) & 1, 0x203)) { ok = false; break; }
           for (int t = 0; t < TILES; ++t) {
             if (j >= w.nkv_t[t]) continue;
-            if (!mbar_wait(&p_full[t], (jt[t] + j) & 1, 0x204)) { ok = false; break; }
-            tc_fence_after();
             // PV_t(0) of an item overwrites O_t: its softmax warpgroup read
             // the previous item's O_t out before this p_full.
-            issue_pv(t, J + j, j > 0);
+            if (!mbar_wait(&p_full[2 * t], (jt[t] + j) & 1, 0x204)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv_half(t, J + j, j > 0, 0);
+            if (!mbar_wait(&p_full[2 * t + 1], (jt[t] + j) & 1, 0x206)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv_half(t, J + j, j > 0, 1);
             if (j + 1 < w.nkv_t[t]) {
               const int s1 = (J + j + 1) % NS;
               if (!mbar_wait(&k_full[s1], ((J + j + 1) / NS) & 1, 0x205)) { ok = false; break; }
@@ -401,49 +412,55 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
         const float m_use = (m == -INFINITY) ? 0.f : m;
         // Packed f32x2 arithmetic halves the instruction count of the scale and
-        // row-sum steps; the exponentials go to MUFU.EX2.
+        // row-sum steps; the exponentials go to MUFU.EX2. P is handed over in
+        // two halves (keys [0, 64), then [64, 128)), so the MMA thread runs
+        // the first half's PV while the second half is exponentiated.
         float2 l2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
         const float2 sl2_2 = make_float2(sl2, sl2), negm2 = make_float2(-m_use, -m_use);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t pk[16];
+        for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc) {
-            const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i][2 * cc]),
-                                                    __uint_as_float(sr[i][2 * cc + 1])),
-                                        sl2_2, negm2);
-            const float2 pp = make_float2(ex2(x.x), ex2(x.y));
-            l2[cc & 3] = __fadd2_rn(l2[cc & 3], pp);
-            pk[cc] = FMT == 1 ? pack_bf16(pp.x, pp.y) : pack_f16(pp.x, pp.y);
+          for (int i = 2 * h; i < 2 * h + 2; ++i) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int cc = 0; cc < 16; ++cc) {
+              const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[i][2 * cc]),
+                                                      __uint_as_float(sr[i][2 * cc + 1])),
+                                          sl2_2, negm2);
+              const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+              l2[cc & 3] = __fadd2_rn(l2[cc & 3], pp);
+              pk[cc] = FMT == 1 ? pack_bf16(pp.x, pp.y) : pack_f16(pp.x, pp.y);
+            }
+#pragma unroll
+            for (int cc = 0; cc < 16; ++cc) sr[h][(i & 1) * 16 + cc] = pk[cc];
           }
+          tmem_st32(lane_addr + t * 128 + 32 * h, sr[h]);
+          // O is rescaled before the first half's PV accumulates into it.
+          // tcgen05.ld/st are warp-collective: if any row of the warp
+          // rescales, the whole warp runs the loop (alpha is 1 for rows that
+          // do not). PV_t(j-1) has completed: s_full(j) follows it in issue
+          // order.
+          if (h == 0 && __any_sync(0xffffffffu, rescale && j > 0)) {
+            const float a = (rescale && j > 0) ? alpha : 1.f;
 #pragma unroll
-          for (int cc = 0; cc < 16; ++cc) sr[i >> 1][(i & 1) * 16 + cc] = pk[cc];
+            for (int i = 0; i < D / 32; ++i) {
+              uint32_t ov[32];
+              tmem_ld32(lane_addr + 256 + t * 128 + 32 * i, ov);
+              tmem_ld_wait();
+#pragma unroll
+              for (int cc = 0; cc < 32; ++cc) ov[cc] = __float_as_uint(__uint_as_float(ov[cc]) * a);
+              tmem_st32(lane_addr + 256 + t * 128 + 32 * i, ov);
+            }
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&p_full[2 * t + h]);
         }
         {
           const float2 a2 = __fadd2_rn(__fadd2_rn(l2[0], l2[1]), __fadd2_rn(l2[2], l2[3]));
           l += a2.x + a2.y;
         }
-        tmem_st32(lane_addr + t * 128, sr[0]);
-        tmem_st32(lane_addr + t * 128 + 32, sr[1]);
-        // tcgen05.ld/st are warp-collective: if any row of the warp rescales,
-        // the whole warp runs the loop (alpha is 1 for rows that do not).
-        // PV_t(j-1) has completed: s_full(j) follows it in issue order.
-        if (__any_sync(0xffffffffu, rescale && j > 0)) {
-          if (!(rescale && j > 0)) alpha = 1.f;
-#pragma unroll
-          for (int i = 0; i < D / 32; ++i) {
-            uint32_t ov[32];
-            tmem_ld32(lane_addr + 256 + t * 128 + 32 * i, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int cc = 0; cc < 32; ++cc) ov[cc] = __float_as_uint(__uint_as_float(ov[cc]) * alpha);
-            tmem_st32(lane_addr + 256 + t * 128 + 32 * i, ov);
-          }
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
       if (nkv_t > 0) {
