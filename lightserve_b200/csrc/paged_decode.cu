@@ -763,6 +763,67 @@ __global__ void rope_kv_write_slots_kernel(const T* __restrict__ qkv, int64_t s_
   }
 }
 
+// 16-byte vectorised form of rope_kv_write_slots_kernel for 16-bit types:
+// a thread rotates 8 consecutive pairs (i, i + D/2) of one head of one token
+// (16-byte loads of q, k, v, cos and sin, 16-byte stores); a 256-thread CTA
+// covers 256 / (H * D / 16) tokens. Same roundings as the scalar kernel.
+template <typename T>
+__global__ void __launch_bounds__(256)
+rope_kv_write_slots_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                               const T* __restrict__ cos_t, const T* __restrict__ sin_t,
+                               int64_t s_pos, const int64_t* __restrict__ positions,
+                               const int64_t* __restrict__ slot_mapping, T* __restrict__ q_out,
+                               T* __restrict__ k_out, T* __restrict__ k_cache,
+                               T* __restrict__ v_cache, int H, int D, int64_t T_tokens,
+                               int64_t num_slots, int bs) {
+  const int half = D / 2;
+  const int lanes_per_token = H * half / 8;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = g / lanes_per_token;
+  if (t >= T_tokens) return;
+  const int r = (int)(g - t * lanes_per_token);
+  const int h = r / (half / 8);
+  const int i0 = (r - h * (half / 8)) * 8;
+  const int64_t pos = positions[t];
+  const int64_t slot = slot_mapping[t];
+  const bool write = slot >= 0 && slot < num_slots;
+  const Vec16<T> c0 = ld_vec16(cos_t + pos * s_pos + i0), c1 = ld_vec16(cos_t + pos * s_pos + i0 + half);
+  const Vec16<T> n0 = ld_vec16(sin_t + pos * s_pos + i0), n1 = ld_vec16(sin_t + pos * s_pos + i0 + half);
+  const T* qh = qkv + t * s_s + h * s_h;
+  const Vec16<T> q1 = ld_vec16(qh + i0), q2 = ld_vec16(qh + i0 + half);
+  const Vec16<T> k1 = ld_vec16(qh + s_part + i0), k2 = ld_vec16(qh + s_part + i0 + half);
+  Vec16<T> oq1, oq2, ok1, ok2;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float fc0 = to_f(c0.v[e]), fc1 = to_f(c1.v[e]), fn0 = to_f(n0.v[e]), fn1 = to_f(n1.v[e]);
+    // rotate_half(x) = [-x2, x1]; every product and sum rounded to T.
+    auto rope = [&](float x1, float x2, T& o1, T& o2) {
+      const float a = to_f(from_f<T>(__fmul_rn(x1, fc0)));
+      const float b = to_f(from_f<T>(__fmul_rn(-x2, fn0)));
+      o1 = from_f<T>(__fadd_rn(a, b));
+      const float c = to_f(from_f<T>(__fmul_rn(x2, fc1)));
+      const float d = to_f(from_f<T>(__fmul_rn(x1, fn1)));
+      o2 = from_f<T>(__fadd_rn(c, d));
+    };
+    rope(to_f(q1.v[e]), to_f(q2.v[e]), oq1.v[e], oq2.v[e]);
+    rope(to_f(k1.v[e]), to_f(k2.v[e]), ok1.v[e], ok2.v[e]);
+  }
+  const int64_t o = (t * H + h) * D + i0;
+  st_vec16(q_out + o, oq1);
+  st_vec16(q_out + o + half, oq2);
+  if (k_out != nullptr) {
+    st_vec16(k_out + o, ok1);
+    st_vec16(k_out + o + half, ok2);
+  }
+  if (write) {
+    const int64_t dst = (((slot / bs) * H + h) * bs + slot % bs) * D + i0;
+    st_vec16(k_cache + dst, ok1);
+    st_vec16(k_cache + dst + half, ok2);
+    st_vec16(v_cache + dst, ld_vec16(qh + 2 * s_part + i0));
+    st_vec16(v_cache + dst + half, ld_vec16(qh + 2 * s_part + i0 + half));
+  }
+}
+
 }  // namespace lsb
 
 extern "C" int lsb_rope_kv_write_slots(const void* qkv, int64_t s_s, int64_t s_part, int64_t s_h,
@@ -779,6 +840,26 @@ extern "C" int lsb_rope_kv_write_slots(const void* qkv, int64_t s_s, int64_t s_p
                 "rope_kv_write_slots: null pointer");
   LSB_CHECK_ARG(T <= 0x7fffffff, "rope_kv_write_slots: T too large");
   cudaStream_t st = (cudaStream_t)stream;
+  const bool a16 = [&] {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return (D % 16) == 0 && al(qkv) && al(cos_table) && al(sin_table) && al(q_out) &&
+           (k_out == nullptr || al(k_out)) && al(k_cache) && al(v_cache) && (s_s * 2) % 16 == 0 &&
+           (s_part * 2) % 16 == 0 && (s_h * 2) % 16 == 0 && (s_pos * 2) % 16 == 0;
+  }();
+  if ((dtype == LSB_DTYPE_BF16 || dtype == LSB_DTYPE_F16) && a16) {
+    const int64_t lanes = T * H * D / 16;
+    const unsigned blocks = (unsigned)((lanes + 255) / 256);
+    auto launch = [&](auto tag) -> int {
+      using Tp = decltype(tag);
+      lsb::rope_kv_write_slots_vec_kernel<Tp><<<blocks, 256, 0, st>>>(
+          (const Tp*)qkv, s_s, s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos,
+          positions, slot_mapping, (Tp*)q_out, (Tp*)k_out, (Tp*)k_cache, (Tp*)v_cache, (int)H,
+          (int)D, T, num_blocks * block_size, (int)block_size);
+      LSB_CHECK_LAUNCH("rope_kv_write_slots");
+      return LSB_OK;
+    };
+    return dtype == LSB_DTYPE_BF16 ? launch(__nv_bfloat16()) : launch(__half());
+  }
   return LSB_DISPATCH_DTYPE(dtype, Tp, [&] {
     lsb::rope_kv_write_slots_kernel<Tp><<<(unsigned)T, 256, 0, st>>>(
         (const Tp*)qkv, s_s, s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos,
