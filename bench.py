@@ -257,6 +257,45 @@ def bench_rmsnorm(steps, warmup, ws, rank):
             "kernel_ms": statistics.mean(per), "launches_per_step": 1}
 
 
+def bench_serving(ws, rank, max_tokens=64):
+    """Continuous batching end to end (ServingEngine: scheduler, packed
+    prefill, CUDA-graph paged decode, host-side token handling each step) on
+    config 5's model and prompt set: all 64 requests submitted at once, each
+    generating max_tokens tokens. Timed on the host around run(), after one
+    warm-up run of the same requests."""
+    from lightserve_b200.engine import CacheConfig, Request, SamplingParams, SchedulerConfig
+    from lightserve_b200.model.minimal_llama import decode_bench_config, init_weights
+    from lightserve_b200.model.serving import ServingEngine
+
+    c = DEC_CFG
+    cfg = decode_bench_config()
+    w = init_weights(cfg, device="cuda", seed=0)
+    g = torch.Generator().manual_seed(rank)
+    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    bs = c["block_size"]
+    blocks = sum(-(-(n + max_tokens) // bs) for n in lens) + 8
+    eng = ServingEngine(w, cfg, CacheConfig(block_size=bs, num_gpu_blocks=blocks),
+                        SchedulerConfig(max_num_seqs=c["S"], max_num_batched_tokens=sum(lens)))
+    times = []
+    for it in range(2):
+        for i, p in enumerate(prompts):
+            eng.add_request(Request(f"run{it}-{i}", p, SamplingParams(max_tokens=max_tokens)))
+        torch.cuda.synchronize()
+        barrier(ws)
+        t0 = time.perf_counter()
+        out = eng.run()
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+        assert len(out) == c["S"] and all(len(v) == max_tokens for v in out.values())
+    el = max_over_ranks(times[-1], ws)
+    gen = c["S"] * max_tokens
+    return {"seconds": el, "requests": c["S"], "prompt_tokens": sum(lens), "generated_tokens": gen,
+            "value": ws * gen / el, "unit": "generated tokens/s",
+            "total_tokens_per_s": ws * (gen + sum(lens)) / el,
+            "note": "host-timed ServingEngine.run(): prefill of every prompt, then decode steps"}
+
+
 def bench_varlen(steps, warmup, ws, rank):
     """Packed (variable-length) causal attention over config 5's prompt set:
     64 sequences with lengths U[512, 4096], 16 heads x 128, bf16 -- one
@@ -419,7 +458,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--only", default="fwd,bwd,rmsnorm,varlen,decode,context",
+    ap.add_argument("--only", default="fwd,bwd,rmsnorm,varlen,decode,serving,context",
                     help="comma list of workloads (fwd is always run: it is the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--strong", action="store_true",
@@ -449,6 +488,8 @@ def main():
                                                              / peaks["bf16_tflops"])
     if "decode" in only:
         secondary["paged_decode"] = bench_decode(min(args.steps * 4, 128), args.warmup, ws, rank)
+    if "serving" in only:
+        secondary["serving"] = bench_serving(ws, rank)
     if ws == 1 and "context" in only:
         try:
             secondary["torch_sdpa_context"] = bench_torch_sdpa(args.steps, args.warmup)

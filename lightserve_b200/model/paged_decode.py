@@ -212,26 +212,46 @@ class PagedDecoder:
         slots[i] processes tokens[i] at positions[i] with block table
         tables[i]; every other row is idle (no block table, so no cache write).
         Returns the greedy next token of each given slot (host ints). The
-        CUDA graph is captured on first use, with every row idle."""
+        CUDA graph is captured on first use, with every row idle.
+
+        Host state lives in pinned buffers; a row's block table is rewritten
+        only when another table takes the row, otherwise only its new
+        entries are appended (block tables grow by appending)."""
         if use_graph and self.graph is None:
             self.block_tables.fill_(-1)
             self.capture()
-        tok = torch.zeros(self.S, dtype=torch.int64)
-        pos = torch.zeros(self.S, dtype=torch.int64)
-        bt = torch.full((self.S, self.MB), -1, dtype=torch.int32)
+        if not hasattr(self, "_h_bt"):
+            self._h_tok = torch.zeros(self.S, dtype=torch.int64).pin_memory()
+            self._h_pos = torch.zeros(self.S, dtype=torch.int64).pin_memory()
+            self._h_bt = torch.full((self.S, self.MB), -1, dtype=torch.int32).pin_memory()
+            self._row_src = [None] * self.S  # table list each row was written from
+            self._row_len = [0] * self.S
+        tok, pos, bt = self._h_tok.numpy(), self._h_pos.numpy(), self._h_bt.numpy()
+        active = set(slots)
+        for s_ in range(self.S):
+            if s_ not in active and self._row_src[s_] is not None:
+                bt[s_, :] = -1
+                self._row_src[s_], self._row_len[s_] = None, 0
+                tok[s_] = pos[s_] = 0
         for s_, t, p_, tb in zip(slots, tokens, positions, tables):
             assert len(tb) <= self.MB, "block table longer than max_blocks_per_seq"
             assert p_ < self.cfg.max_seq_len, "position beyond the RoPE table"
             tok[s_], pos[s_] = t, p_
-            bt[s_, :len(tb)] = torch.tensor(tb, dtype=torch.int32)
-        self.tokens.copy_(tok, non_blocking=True)
-        self.positions.copy_(pos, non_blocking=True)
-        self.block_tables.copy_(bt, non_blocking=True)
+            n0 = self._row_len[s_]
+            if self._row_src[s_] is not tb or len(tb) < n0:
+                bt[s_, :] = -1
+                n0 = 0
+            if len(tb) > n0:
+                bt[s_, n0:len(tb)] = tb[n0:]
+            self._row_src[s_], self._row_len[s_] = tb, len(tb)
+        self.tokens.copy_(self._h_tok, non_blocking=True)
+        self.positions.copy_(self._h_pos, non_blocking=True)
+        self.block_tables.copy_(self._h_bt, non_blocking=True)
         if use_graph:
             self.graph.replay()
         else:
             self.step()
-        nxt = self.tokens.cpu()
+        nxt = self.tokens.cpu()  # also orders the next step's host writes after these copies
         return [int(nxt[s_]) for s_ in slots]
 
     # ----------------------------------------------------------------- step --

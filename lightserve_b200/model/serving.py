@@ -83,7 +83,8 @@ class ServingEngine:
         run = [x.request for x in out.scheduled_running]
         if run:
             toks = self.runner.decode_slots(
-                [self.slot_of[r.request_id] for r in run], [r.all_token_ids()[-1] for r in run],
+                [self.slot_of[r.request_id] for r in run],
+                [r.output_token_ids[-1] if r.output_token_ids else r.prompt_token_ids[-1] for r in run],
                 [r.get_len() - 1 for r in run], [bm.get_block_table(r) for r in run],
                 use_graph=self.use_graph)
             self.num_decode_tokens += len(run)
