@@ -51,6 +51,17 @@ LSB_API const char* lsb_last_error(void);
  * synchronises the device. 0 when no kernel ever timed out. */
 LSB_API int lsb_device_error(void);
 
+/* Returns lsb_device_error() and clears every error word. No counterpart in
+ * the reference (its Triton kernels have no bounded waits). */
+LSB_API int lsb_device_error_reset(void);
+
+/* Self-test of the bounded-wait failure path: launches one thread that waits
+ * on an mbarrier nothing arrives on; after about one second the wait gives
+ * up, the kernel writes *status = 0 (device int) and lsb_device_error()
+ * returns 0xE01. The GPU context stays usable. No counterpart in the
+ * reference. */
+LSB_API int lsb_selftest_bounded_wait(int* status, void* stream);
+
 /* Library version string. */
 LSB_API const char* lsb_version(void);
 

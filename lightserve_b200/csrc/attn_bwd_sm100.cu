@@ -800,10 +800,8 @@ extern "C" LSB_API int lsb_bwd_item_read(unsigned long long* out) {
 }
 #endif
 
-int attn_bwd_tc_device_error() {
-  int e = 0;
-  cudaMemcpyFromSymbol(&e, sm100::g_lsb_device_error, sizeof(int));
-  return e;
+int attn_bwd_tc_device_error(bool reset) {
+  return sm100::tu_device_error(reset);
 }
 
 }  // namespace lsb

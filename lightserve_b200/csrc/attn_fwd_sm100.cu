@@ -614,10 +614,8 @@ int attn_fwd_varlen_tc(const void* q, const void* k, const void* v, void* o, flo
                                    cu_seqlens, n_seqs, max_seqlen);
 }
 
-int attn_fwd_tc_device_error() {
-  int e = 0;
-  cudaMemcpyFromSymbol(&e, sm100::g_lsb_device_error, sizeof(int));
-  return e;
+int attn_fwd_tc_device_error(bool reset) {
+  return sm100::tu_device_error(reset);
 }
 
 }  // namespace lsb

@@ -52,21 +52,27 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
                 const int64_t* sdv, float scale, int causal, int dtype, float* dsum,
                 float* dq_acc, cudaStream_t st);
 
-int attn_fwd_tc_device_error();
-int attn_bwd_tc_device_error();
-int paged_decode_device_error();
+int attn_fwd_tc_device_error(bool reset);
+int attn_bwd_tc_device_error(bool reset);
+int paged_decode_device_error(bool reset);
+int selftest_device_error(bool reset);
 
 
 }  // namespace lsb
 
 extern "C" const char* lsb_last_error(void) { return lsb::g_err; }
 
-extern "C" int lsb_device_error(void) {
-  int e = lsb::attn_fwd_tc_device_error();
-  if (!e) e = lsb::attn_bwd_tc_device_error();
-  if (!e) e = lsb::paged_decode_device_error();
+static int device_error_all(bool reset) {
+  int e = 0;
+  for (int v : {lsb::attn_fwd_tc_device_error(reset), lsb::attn_bwd_tc_device_error(reset),
+                lsb::paged_decode_device_error(reset), lsb::selftest_device_error(reset)})
+    if (!e) e = v;
   return e;
 }
+
+extern "C" int lsb_device_error(void) { return device_error_all(false); }
+
+extern "C" int lsb_device_error_reset(void) { return device_error_all(true); }
 
 extern "C" const char* lsb_version(void) { return "lightserve_b200 0.1 (sm_100a)"; }
 

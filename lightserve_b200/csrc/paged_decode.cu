@@ -464,10 +464,8 @@ __global__ void kv_cache_write_kernel(const T* __restrict__ k, const T* __restri
   }
 }
 
-int paged_decode_device_error() {
-  int e = 0;
-  cudaMemcpyFromSymbol(&e, sm100::g_lsb_device_error, sizeof(int));
-  return e;
+int paged_decode_device_error(bool reset) {
+  return sm100::tu_device_error(reset);
 }
 
 }  // namespace lsb

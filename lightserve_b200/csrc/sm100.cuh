@@ -24,6 +24,17 @@ namespace sm100 {
 // each unit exposes a host reader that lsb_device_error() combines.
 static __device__ int g_lsb_device_error = 0;
 
+// Host side: this translation unit's error word (and optionally clear it).
+static inline int tu_device_error(bool reset) {
+  int e = 0;
+  cudaMemcpyFromSymbol(&e, g_lsb_device_error, sizeof(int));
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_lsb_device_error, &z, sizeof(int));
+  }
+  return e;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
