@@ -34,6 +34,9 @@ extern "C" {
 #define LSB_ERR_UNSUPPORTED 2 /* valid request this build cannot serve     */
 #define LSB_ERR_CUDA 3        /* a CUDA runtime call or launch failed      */
 
+/* lsb_device_error(): the device error words could not be read. */
+#define LSB_DEVICE_ERR_QUERY 0xCDA
+
 #define LSB_DTYPE_F32 0
 #define LSB_DTYPE_BF16 1
 #define LSB_DTYPE_F16 2
@@ -48,7 +51,9 @@ LSB_API const char* lsb_last_error(void);
 
 /* Nonzero if a kernel of this library gave up on a bounded on-chip wait (an
  * mbarrier that never completed); the value names the wait. Reading it
- * synchronises the device. 0 when no kernel ever timed out. */
+ * synchronises the device. 0 when no kernel ever timed out.
+ * LSB_DEVICE_ERR_QUERY when the error words could not be read at all (the
+ * CUDA context holds an error; lsb_last_error() names it). */
 LSB_API int lsb_device_error(void);
 
 /* Returns lsb_device_error() and clears every error word. No counterpart in

@@ -6,3 +6,14 @@ Operators (drop-ins for lightserve's ``kernels/`` call sites) live in
 All compute goes through liblightserve_b200.so (include/lightserve_b200.h).
 """
 __version__ = "0.1.0"
+
+
+from ._lib import DeviceWaitError  # noqa: E402
+
+
+def check_device_errors(reset: bool = True) -> None:
+    """Raises if a kernel of the library gave up on a bounded on-chip wait
+    (see ``lightserve_b200._lib.check_device_errors``)."""
+    from ._lib import check_device_errors as _check
+
+    _check(reset)

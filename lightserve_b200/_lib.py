@@ -138,3 +138,28 @@ def device_guard(device: torch.device):
 
 def stream_ptr(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class DeviceWaitError(RuntimeError):
+    """A kernel of the library gave up on a bounded on-chip wait; the outputs
+    of the launches since the last check are not trustworthy."""
+
+    def __init__(self, code: int):
+        self.code = code
+        what = ("the device error words could not be read: " + last_error()
+                if code == LSB_DEVICE_ERR_QUERY else f"a bounded wait gave up (code {code:#x})")
+        super().__init__(f"lightserve_b200 device error: {what}")
+
+
+LSB_DEVICE_ERR_QUERY = 0xCDA
+
+
+def check_device_errors(reset: bool = True) -> None:
+    """Raises DeviceWaitError if any kernel of the library timed out on an
+    on-chip wait since the last reset (by default the error words are cleared
+    when read, so each error is reported once). Synchronises the current
+    device: call it at step or test boundaries, not between launches."""
+    lib = load()
+    code = lib.lsb_device_error_reset() if reset else lib.lsb_device_error()
+    if code != 0:
+        raise DeviceWaitError(int(code))

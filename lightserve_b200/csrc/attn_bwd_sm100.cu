@@ -108,33 +108,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-#ifdef LSB_BWD_TRACE
-// Debug-build timeline of the first work item of CTA 0: clock64 per event and
-// query tile; per work item: global timer at start / first S^T / end, SM id, tiles.
-__device__ long long g_bwd_trace[16][64];
-__device__ unsigned long long g_bwd_cta[8192][5];
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define BWD_TRACE(cond, ev, it)                                               \
-  do {                                                                        \
-    if ((cond) && blockIdx.x == 0 && (it) < 64) g_bwd_trace[ev][it] = clock64(); \
-  } while (0)
-#define BWD_ITEM(item, slot, val)                                             \
-  do {                                                                        \
-    if ((item) < 8192) g_bwd_cta[item][slot] = (val);                         \
-  } while (0)
-#else
-#define BWD_TRACE(cond, ev, it) \
-  do {                          \
-  } while (0)
-#define BWD_ITEM(item, slot, val) \
-  do {                            \
-  } while (0)
-#endif
-
 template <int FMT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   return FMT == 1 ? pack_bf16(a, b) : pack_f16(a, b);
@@ -318,7 +291,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     int item = claim(0);
     for (int k = 0; ok && item >= 0 && item < n_items; ++k) {
       const Item w = decode_item(item, p);
-      BWD_ITEM(item, 0, gtimer());
       const float* lse_bh = p.lse + (int64_t)w.bh * p.N;
       const float* dsum_bh = p.dsum + (int64_t)w.bh * p.N;
       int next = -1;
@@ -350,7 +322,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           st[BM + c] = in ? __ldg(dsum_bh + m0 + c) : 0.f;
         }
         mbar_arrive(&stat_full[s]);
-        BWD_TRACE(lane == 0, 0, g);
         // K of this item replaces the previous item's once its last dQ^T
         // (the last reader of K) has completed.
         if (it == 0) {
@@ -366,7 +337,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         // dO(g-1) once dV(g-1) has read it.
         if (it == 0 && k > 0 && !mbar_wait_warp(epi_v_free, (k - 1) & 1, 0x503)) { ok = false; break; }
         if (g > 0 && !mbar_wait_warp(do_empty, (g - 1) & 1, 0x502)) { ok = false; break; }
-        BWD_TRACE(lane == 0, 3, g);
         if (lane == 0) {
           if (it == 0) {
             mbar_arrive_expect_tx(v_full, TILE);
@@ -427,14 +397,12 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tc_fence_after();
         issue_t(T_S, k_base, q_base + s * TILE);
         mma_commit(s_ready);
-        BWD_TRACE(true, 1, gg);
         if ((gg > 0 && !mbar_wait(dq_free, (gg - 1) & 1, 0x606)) ||
             !mbar_wait(do_full, gg & 1, 0x608) || (first && !mbar_wait(v_full, k & 1, 0x609)))
           return false;
         tc_fence_after();
         issue_t(T_DP, v_base, do_base);
         mma_commit(dp_ready);
-        BWD_TRACE(true, 6, gg);
         return true;
       };
       int g = 0;
@@ -450,12 +418,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           // dV(0) of an item overwrites the previous item's dV: the
           // warpgroups read it out (epilogue) before their p_ready.
           if (!mbar_wait(p_ready, ph, 0x603)) { ok = false; break; }
-          BWD_TRACE(true, 2, g);
           tc_fence_after();
           issue_acc(T_DV, 0, do_base, it > 0);
           mma_commit(do_empty);
           if (!mbar_wait(ds_ready, ph, 0x604)) { ok = false; break; }
-          BWD_TRACE(true, 4, g);
           tc_fence_after();
           // dQ^T(g) = K^T dS^T over the 128 keys, into the dP^T columns
           // (every read of dP^T(g) preceded ds_ready).
@@ -470,7 +436,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           issue_acc(T_DK, 32, q_base + s * TILE, it > 0);
           mma_commit(dk_done);
           mma_commit(&q_empty[s]);
-          BWD_TRACE(true, 5, g);
           // tcgen05.mma instructions of one thread execute in issue order, so
           // S^T(g+1) overwrites P^T / dS^T(g) only after dV(g) and dK(g)
           // have read them.
@@ -504,13 +469,11 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             // has been read by now).
             ok = mbar_wait(epi_staged, kk & 1, 0x902);
             if (!ok) break;
-            BWD_TRACE(true, 13, g);
             for (int kc = 0; kc < KC; ++kc)
               tma_store_4d(&tdk, sV + kc * CHUNK, kc * 64, w.kv0, w.h, w.b);
             bulk_commit();
             bulk_wait_read();
             mbar_arrive(epi_v_free);
-            BWD_TRACE(true, 14, g);
             ok = mbar_wait(vdo_issued, kk & 1, 0x903);
             if (!ok) break;
             for (int kc = 0; kc < KC; ++kc)
@@ -529,7 +492,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
           if (last) {
             bulk_wait_read_2();
             mbar_arrive(&epi_q_free[g % NQS]);
-            BWD_TRACE(true, 15, g);
           }
           bulk_wait_read_1();
           mbar_arrive(&red_free[1]);
@@ -570,8 +532,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         const float* st = stats + (g % NQS) * 2 * BM;
         if (!mbar_wait_warp(&stat_full[g % NQS], (g / NQS) & 1, 0x705)) { ok = false; break; }
         if (!mbar_wait_warp(s_ready, ph, 0x701)) { ok = false; break; }
-        BWD_TRACE(r == 0 && half == 0, 7, g);
-        if (it == 0 && r == 0 && half == 0) BWD_ITEM(item, 1, gtimer());
         tc_fence_after();
         uint32_t sv[64];
         tmem_ld32(my_s, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
@@ -605,10 +565,8 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(p_ready);
-        BWD_TRACE(r == 0 && half == 0, 8, g);
 
         if (!mbar_wait_warp(dp_ready, ph, 0x702)) { ok = false; break; }
-        BWD_TRACE(r == 0 && half == 0, 9, g);
         tc_fence_after();
         tmem_ld32(lane_addr + T_DP + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         tmem_ld32(lane_addr + T_DP + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
@@ -635,11 +593,9 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(ds_ready);
-        BWD_TRACE(r == 0 && half == 0, 10, g);
 
         // dQ^T(g), thread = head-dim index r, this half's 64 query columns.
         if (!mbar_wait_warp(dq_ready, ph, 0x704)) { ok = false; break; }
-        BWD_TRACE(r == 0 && half == 0, 11, g);
         tc_fence_after();
         tmem_ld32(lane_addr + T_DP + cb, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         tmem_ld32(lane_addr + T_DP + cb + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
@@ -657,7 +613,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         for (int c = 0; c < 64; ++c) stage[c * D + r] = __uint_as_float(sv[c]) * p.scale;
         fence_proxy_async_smem();
         mbar_arrive(&red_full[half]);
-        BWD_TRACE(r == 0 && half == 0, 12, g);
       }
       if (!ok) break;
       // Item epilogue: warpgroup 1 stages this key's dV row (in the last
@@ -692,15 +647,6 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(epi_staged);
-      if (r == 0 && half == 0) BWD_ITEM(item, 2, gtimer());
-#ifdef LSB_BWD_TRACE
-      if (r == 0 && half == 0) {
-        unsigned smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        BWD_ITEM(item, 3, smid);
-        BWD_ITEM(item, 4, w.n);
-      }
-#endif
     }
   }
 
@@ -756,8 +702,8 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   auto kern = fa_bwd_kernel<FMT>;
-  LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM),
-              "attn_bwd_tc smem attribute");
+  static SmemLimit smem_limit;
+  if (int rc_ = smem_limit.ensure(kern, SMEM, "attn_bwd_tc smem attribute")) return rc_;
   // Persistent: one CTA per SM (shared memory and TMEM allow no more).
   const int64_t n_items = B * H * ((N + BN - 1) / BN);
   dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));
@@ -791,14 +737,6 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
             : launch_dq_cast<__half>(dq_acc, dq, B, H, N, D, S4(sdq), st);
 }
 
-#ifdef LSB_BWD_TRACE
-extern "C" LSB_API int lsb_bwd_trace_read(long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, fa_bwd::g_bwd_trace, sizeof(fa_bwd::g_bwd_trace));
-}
-extern "C" LSB_API int lsb_bwd_item_read(unsigned long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, fa_bwd::g_bwd_cta, sizeof(fa_bwd::g_bwd_cta));
-}
-#endif
 
 int attn_bwd_tc_device_error(bool reset) {
   return sm100::tu_device_error(reset);

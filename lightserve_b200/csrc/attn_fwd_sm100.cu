@@ -555,25 +555,36 @@ static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   p.num_q_ctas = (int)((rows + TILES * BM - 1) / (TILES * BM));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
-  // Work-item counter: a slot of g_work_counters per launch (rotating, so
-  // launches in flight on other streams use other slots), zeroed in stream
-  // order just before the kernel (also when captured into a CUDA graph).
-  static int* counters[64] = {nullptr};
-  int dev = 0;
-  LSB_CUDA_OK(cudaGetDevice(&dev), "attn_fwd_tc device");
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (counters[dev] == nullptr) {
+  // Work-item counter: a slot of g_work_counters per launch, zeroed in stream
+  // order just before the kernel. Eager launches rotate through the first
+  // half of the slots, so launches in flight on other streams use other
+  // slots. A launch recorded into a CUDA graph keeps its slot for every
+  // replay, so recorded launches take slots from the second half instead and
+  // never share one with an eager launch (only 128 or more recorded launches
+  // replayed concurrently with each other could collide).
+  const int dev = current_device("attn_fwd_tc");
+  if (dev < 0) return LSB_ERR_CUDA;
+  static int* counters[kMaxDevices] = {nullptr};
+  static PerDeviceOnce counter_lookup;
+  LSB_CUDA_OK(counter_lookup.run(dev, [&] {
     void* addr = nullptr;
-    LSB_CUDA_OK(cudaGetSymbolAddress(&addr, g_work_counters), "attn_fwd_tc counter symbol");
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_work_counters);
     counters[dev] = static_cast<int*>(addr);
-  }
-  static std::atomic<unsigned> next_slot{0};
-  p.work_counter = counters[dev] + (next_slot.fetch_add(1, std::memory_order_relaxed) % COUNTER_SLOTS);
+    return e;
+  }), "attn_fwd_tc counter symbol");
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  LSB_CUDA_OK(cudaStreamIsCapturing(st, &cap), "attn_fwd_tc capture status");
+  static std::atomic<unsigned> next_eager{0}, next_captured{0};
+  constexpr unsigned HALF = COUNTER_SLOTS / 2;
+  const unsigned slot = cap == cudaStreamCaptureStatusNone
+                            ? next_eager.fetch_add(1, std::memory_order_relaxed) % HALF
+                            : HALF + next_captured.fetch_add(1, std::memory_order_relaxed) % HALF;
+  p.work_counter = counters[dev] + slot;
   LSB_CUDA_OK(cudaMemsetAsync(p.work_counter, 0, sizeof(int), st), "attn_fwd_tc counter reset");
   const int smem = Smem<D>::ALLOC;
   auto kern = fa_fwd_kernel<D, FMT>;
-  LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-              "attn_fwd_tc smem attribute");
+  static SmemLimit smem_limit;
+  if (int rc_ = smem_limit.ensure(kern, smem, "attn_fwd_tc smem attribute")) return rc_;
   // Persistent: one CTA per SM (shared memory and TMEM allow no more).
   const int64_t n_items = (int64_t)p.BH * p.num_q_ctas;
   dim3 grid((unsigned)std::min<int64_t>(n_items, num_sms()));

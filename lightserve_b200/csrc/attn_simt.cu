@@ -149,9 +149,8 @@ static int launch_fwd_simt(const void* q, const void* k, const void* v, void* o,
                            cudaStream_t st) {
   const int Dp = (int)((D + 7) / 8 * 8);
   const size_t smem = sizeof(float) * (size_t)(FS_BM * Dp + 2 * FS_BN * Dp + FS_BM * FS_BN);
-  LSB_CUDA_OK(cudaFuncSetAttribute(attn_fwd_simt_kernel<T>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-              "attn_fwd_simt smem attribute");
+  static SmemLimit smem_limit;
+  if (int rc_ = smem_limit.ensure(attn_fwd_simt_kernel<T>, smem, "attn_fwd_simt smem attribute")) return rc_;
   dim3 grid((unsigned)((N + FS_BM - 1) / FS_BM), (unsigned)(B * H));
   attn_fwd_simt_kernel<T><<<grid, FS_THREADS, smem, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (T*)o, lse, (int)H, (int)N, (int)D, Dp, sq, sk, sv,
@@ -436,9 +435,8 @@ static int launch_bwd_simt(const void* q, const void* k, const void* v, const vo
   const int Dp = (int)((D + 7) / 8 * 8);
   const size_t smem =
       sizeof(float) * (size_t)(2 * BS_BN * Dp + 2 * BS_BM * Dp + 2 * BS_BM * BS_BN + 2 * BS_BM);
-  LSB_CUDA_OK(cudaFuncSetAttribute(attn_bwd_simt_kernel<T>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-              "attn_bwd_simt smem attribute");
+  static SmemLimit smem_limit;
+  if (int rc_ = smem_limit.ensure(attn_bwd_simt_kernel<T>, smem, "attn_bwd_simt smem attribute")) return rc_;
   dim3 grid((unsigned)((N + BS_BN - 1) / BS_BN), (unsigned)(B * H));
   attn_bwd_simt_kernel<T><<<grid, BS_THREADS, smem, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, dsum, dq_acc, (T*)dk, (T*)dv,

@@ -67,6 +67,8 @@ static int device_error_all(bool reset) {
   for (int v : {lsb::attn_fwd_tc_device_error(reset), lsb::attn_bwd_tc_device_error(reset),
                 lsb::paged_decode_device_error(reset), lsb::selftest_device_error(reset)})
     if (!e) e = v;
+  if (e == LSB_DEVICE_ERR_QUERY)
+    lsb::set_error("device error words unreadable: %s", cudaGetErrorString(cudaGetLastError()));
   return e;
 }
 

@@ -14,6 +14,9 @@
 #include <stdio.h>
 #include <stdarg.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/lightserve_b200.h"
 
 namespace lsb {
@@ -48,11 +51,69 @@ void set_error(const char* fmt, ...);
     }                                                                             \
   } while (0)
 
+// Per-device state is kept for device ordinals [0, kMaxDevices).
+constexpr int kMaxDevices = 64;
+
+// The current device, or -1 (with the error message set) when it cannot be
+// read or lies outside [0, kMaxDevices).
+inline int current_device(const char* who) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("%s: no usable current device (%s, ordinal %d)", who,
+              e == cudaSuccess ? "ordinal out of range" : cudaGetErrorString(e), dev);
+    return -1;
+  }
+  return dev;
+}
+
+// Runs a set-up step once per device, thread-safely; a failed step is retried
+// on the next call.
+class PerDeviceOnce {
+ public:
+  template <class F>
+  cudaError_t run(int dev, F&& fn) {
+    const uint64_t bit = 1ull << dev;
+    if (done_.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+    const cudaError_t e = fn();
+    if (e == cudaSuccess) done_.fetch_or(bit, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::atomic<uint64_t> done_{0};
+  std::mutex mu_;
+};
+
+// A kernel's dynamic shared-memory limit per device: cudaFuncSetAttribute is
+// called only when a launch needs more than the limit already set on the
+// current device. One static instance per kernel, owned by its launcher.
+class SmemLimit {
+ public:
+  template <class K>
+  int ensure(K kern, size_t bytes, const char* what) {
+    const int dev = current_device(what);
+    if (dev < 0) return LSB_ERR_CUDA;
+    if ((size_t)set_[dev].load(std::memory_order_acquire) >= bytes) return LSB_OK;
+    std::lock_guard<std::mutex> lock(mu_);
+    if ((size_t)set_[dev].load(std::memory_order_relaxed) >= bytes) return LSB_OK;
+    LSB_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                what);
+    set_[dev].store((int)bytes, std::memory_order_release);
+    return LSB_OK;
+  }
+
+ private:
+  std::atomic<int> set_[kMaxDevices] = {};
+  std::mutex mu_;
+};
+
 inline int num_sms() {
-  static int cached[64] = {0};
+  static int cached[kMaxDevices] = {0};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
   if (cached[dev] == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);

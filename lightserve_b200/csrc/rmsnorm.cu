@@ -34,13 +34,8 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
     if (c < nvec) {
-#ifdef LSB_RMS_PLAIN_LD
-      Vec16<T> a = ld_vec16(xr + c * VEC);
-      Vec16<T> b = ld_vec16(rr + c * VEC);
-#else
       Vec16<T> a = ld_vec16_stream(xr + c * VEC);
       Vec16<T> b = ld_vec16_stream(rr + c * VEC);
-#endif
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
         T h = from_f<T>(to_f(a.v[j]) + to_f(b.v[j]));
@@ -76,13 +71,8 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
 #pragma unroll
       for (int j = 0; j < VEC; ++j)
         ov.v[j] = from_f<T>(to_f(hv[i].v[j]) * rrms * to_f(wv.v[j]));
-#ifdef LSB_RMS_PLAIN_ST
-      *reinterpret_cast<uint4*>(hrow + c * VEC) = *reinterpret_cast<uint4*>(&hv[i]);
-      *reinterpret_cast<uint4*>(orow + c * VEC) = *reinterpret_cast<uint4*>(&ov);
-#else
       __stcs(reinterpret_cast<uint4*>(hrow + c * VEC), *reinterpret_cast<uint4*>(&hv[i]));
       __stcs(reinterpret_cast<uint4*>(orow + c * VEC), *reinterpret_cast<uint4*>(&ov));
-#endif
     }
   }
 }

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/lightserve_b200.h"
+
 namespace lsb {
 namespace sm100 {
 
@@ -25,12 +27,16 @@ namespace sm100 {
 static __device__ int g_lsb_device_error = 0;
 
 // Host side: this translation unit's error word (and optionally clear it).
+// When the word itself cannot be read or cleared (for example the context
+// already holds a sticky error), returns LSB_DEVICE_ERR_QUERY instead of 0.
 static inline int tu_device_error(bool reset) {
   int e = 0;
-  cudaMemcpyFromSymbol(&e, g_lsb_device_error, sizeof(int));
+  if (cudaMemcpyFromSymbol(&e, g_lsb_device_error, sizeof(int)) != cudaSuccess)
+    return LSB_DEVICE_ERR_QUERY;
   if (reset) {
     const int z = 0;
-    cudaMemcpyToSymbol(g_lsb_device_error, &z, sizeof(int));
+    if (cudaMemcpyToSymbol(g_lsb_device_error, &z, sizeof(int)) != cudaSuccess)
+      return LSB_DEVICE_ERR_QUERY;
   }
   return e;
 }

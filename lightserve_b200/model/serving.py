@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import torch
 
+from .._lib import check_device_errors
 from ..engine import CacheConfig, Request, Scheduler, SchedulerConfig
 from .minimal_llama import LlamaConfig, LlamaWeights
 from .paged_decode import PagedDecoder, PagedKVCache
@@ -28,8 +29,14 @@ from .paged_decode import PagedDecoder, PagedKVCache
 
 class ServingEngine:
     def __init__(self, weights: LlamaWeights, config: LlamaConfig, cache_config: CacheConfig,
-                 scheduler_config: SchedulerConfig, device="cuda", use_graph: bool = True):
+                 scheduler_config: SchedulerConfig, device="cuda", use_graph: bool = True,
+                 check_every: int = 64):
         self.cfg = config
+        # Every `check_every` steps (and at the end of run()) the device error
+        # words are read: a kernel that gave up on a bounded wait raises
+        # lightserve_b200.DeviceWaitError instead of yielding tokens silently.
+        self.check_every = check_every
+        self._steps = 0
         self.scheduler = Scheduler(cache_config, scheduler_config)
         bs = cache_config.block_size
         self.cache = PagedKVCache(config, cache_config.num_gpu_blocks, bs, device=device)
@@ -93,6 +100,9 @@ class ServingEngine:
         done = self.scheduler.free_finished_requests()
         for r in done:
             self._release(r)
+        self._steps += 1
+        if self.check_every and self._steps % self.check_every == 0:
+            check_device_errors()
         return done
 
     def run(self, max_steps: int = 1_000_000) -> dict:
@@ -104,6 +114,7 @@ class ServingEngine:
             for r in self.step():
                 results[r.request_id] = list(r.output_token_ids)
         assert not self.has_unfinished_requests(), "max_steps reached with requests unfinished"
+        check_device_errors()
         return results
 
     def generate(self, prompts, max_tokens: int, eos_token_id=None) -> list:

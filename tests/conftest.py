@@ -24,3 +24,20 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_wait_errors(request):
+    """After every GPU test: no kernel of the library may have given up on a
+    bounded on-chip wait (such a kernel ends with partial output, so a test
+    that passed on it would prove nothing)."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from lightserve_b200 import check_device_errors
+
+    check_device_errors(reset=True)

@@ -1,7 +1,7 @@
 """Generates the golden fixtures in tests/golden/ from lightserve's own code.
 
 Run in a container where the lightserve sources are available (path given by
---reference, default /root/reference); the fixtures it writes are small .npz
+--reference, a required argument); the fixtures it writes are small .npz
 files committed next to this script, so tests never need the reference.
 
 What it records:
@@ -139,7 +139,7 @@ def gen_llama(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the lightserve source tree")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(min(8, os.cpu_count() or 1))

@@ -36,3 +36,21 @@ def test_bounded_wait_gives_up_and_context_stays_usable():
     torch.testing.assert_close(out.cpu(), eo, atol=2e-2, rtol=2e-2)
     assert lib.lsb_device_error_reset() == 0xE01
     assert lib.lsb_device_error() == 0
+
+
+def test_operator_after_timed_out_wait_raises_through_check():
+    """A bounded wait that gave up is reported by check_device_errors() (and
+    by ServingEngine / bench.py, which call it), once, then cleared."""
+    from lightserve_b200 import check_device_errors
+    from lightserve_b200._lib import DeviceWaitError
+
+    lib = _lib.load()
+    check_device_errors()
+    status = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    assert lib.lsb_selftest_bounded_wait(status.data_ptr(), _lib.stream_ptr(status.device)) == 0
+    x, r = (torch.randn(8, 512, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    fused_add_rmsnorm(x, r, torch.ones(512, device="cuda", dtype=torch.bfloat16), 1e-6)
+    with pytest.raises(DeviceWaitError) as ei:
+        check_device_errors()
+    assert ei.value.code == 0xE01
+    check_device_errors()  # cleared by the read above
