@@ -6,9 +6,14 @@ convention 4*B*H*N^2*D/2 (kernels/benchmark_flash_attention.py:55-64).
 Secondary lines in the same JSON object: FA backward (config 3), fused
 add+RMSNorm (config 4) and paged greedy decode tokens/s (config 5).
 
-Multi-GPU: one process per GPU (torchrun); every rank runs the full per-GPU
-workload on its own (batch x head) slices -- independent units, no
-collective on the data path ("scaling": "weak"); times are the max over ranks.
+Multi-GPU: one process per GPU (torchrun). By default each configuration's
+fixed total work is partitioned across the ranks ("scaling": "strong"):
+config 2's and config 3's 128 (batch x head) slices, config 4's rows, config
+5's 64 sequences (each rank holds a full weight replica, its own paged KV
+pool and its own CUDA graph). The units are independent, so there is no
+collective on the data path; times are the max over ranks and every value is
+the whole configuration's work divided by that time. `--scaling weak` gives
+every rank a full configuration instead.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -80,6 +85,31 @@ def max_over_ranks(x: float, ws: int) -> float:
     from lightserve_b200.sharding import max_over_ranks as _m
 
     return _m(x) if ws > 1 else x
+
+
+def _sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+DEVICE_ERRORS: dict = {}
+
+
+def check_device_errors(what: str) -> None:
+    """Reads (and clears) the library's device error words after a workload:
+    a kernel that gave up on a bounded on-chip wait fails the bench loudly
+    instead of reporting a speed for partial output."""
+    from lightserve_b200 import _lib
+
+    code = int(_lib.load().lsb_device_error_reset())
+    DEVICE_ERRORS[what] = code
+    if code:
+        raise RuntimeError(f"{what}: a kernel gave up on a bounded wait (device error {code:#x})")
 
 
 def load_peaks():
@@ -186,7 +216,7 @@ def _randn(shape, dtype, gen):
     return torch.randn(*shape, device="cuda", dtype=torch.float32, generator=gen).to(dtype)
 
 
-def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
+def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=True):
     from lightserve_b200.kernels import flash_attention_forward, flash_attention_forward_host
     from lightserve_b200.sharding import shard_range
 
@@ -199,7 +229,7 @@ def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
         shape = (c["B"], c["H"], c["N"], c["D"])
     q, k, v = (_randn(shape, torch.bfloat16, gen) for _ in range(3))
     flops = attn_fwd_flops(shape[0], shape[1], c["N"], c["D"], c["causal"])
-    mult = 1 if strong else ws  # whole-job work = per-rank work x ranks (weak)
+    job_flops = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) * (1 if strong else ws)
     total_ms, per = time_cuda(lambda: flash_attention_forward(q, k, v, causal=True), steps, warmup, ws)
     ms = total_ms / steps
     kern_ms = statistics.mean(per)
@@ -215,54 +245,77 @@ def bench_fwd(steps, warmup, ws, rank, peaks, e2e_steps, strong=False):
 
     e2e_total, _ = time_cuda(e2e_step, e2e_steps, 1, ws)
     nb = q.numel() * q.element_size()
+    check_device_errors("attention forward")
     return {
-        "ms": ms, "kernel_ms": kern_ms, "flops": flops,
-        "value": (attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) if strong else mult * flops)
-        / (ms * 1e-3) / 1e12,
+        "ms": ms, "kernel_ms": kern_ms, "flops": flops, "slices_per_rank": shape[0] * shape[1],
+        "value": job_flops / (ms * 1e-3) / 1e12,
         "kernel_tflops": flops / (kern_ms * 1e-3) / 1e12,
-        "e2e": {"value": (attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) if strong else mult * flops)
-                / (e2e_total / e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "e2e": {"value": job_flops / (e2e_total / e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 3 * nb, "d2h_bytes_per_step": nb, "steps": e2e_steps},
         "launches_per_step": 1,
     }
 
 
-def bench_bwd(steps, warmup, ws, rank):
+def bench_bwd(steps, warmup, ws, rank, strong=True):
     from lightserve_b200.kernels.flash_attention_backward import (_flash_attention_backward,
                                                                   _flash_attention_forward_lse)
+    from lightserve_b200.sharding import shard_range
 
     c = BWD_CFG
     gen = torch.Generator(device="cuda").manual_seed(2000 + rank)
-    q, k, v, do = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(4))
+    if strong:
+        a, b = shard_range(c["B"] * c["H"], rank, ws)
+        shape = (1, b - a, c["N"], c["D"])
+    else:
+        shape = (c["B"], c["H"], c["N"], c["D"])
+    q, k, v, do = (_randn(shape, torch.bfloat16, gen) for _ in range(4))
     o, L = _flash_attention_forward_lse(q, k, v, True)
-    flops = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True)
+    job_flops = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) * (1 if strong else ws)
     total_ms, per = time_cuda(lambda: _flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, ws)
     ms = total_ms / steps
-    return {"ms": ms, "flops": flops, "value": ws * flops / (ms * 1e-3) / 1e12,
-            "unit": "TFLOP/s", "launches_per_step": 3}
+    check_device_errors("attention backward")
+    return {"ms": ms, "flops": job_flops, "value": job_flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "launches_per_step": 3, "slices_per_rank": shape[0] * shape[1]}
 
 
-def bench_rmsnorm(steps, warmup, ws, rank):
+def bench_rmsnorm(steps, warmup, ws, rank, strong=True):
     from lightserve_b200.kernels import fused_add_rmsnorm
+    from lightserve_b200.sharding import shard_range
 
     c = RMS_CFG
     gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
-    x = _randn((c["M"], c["N"]), torch.bfloat16, gen)
-    r = _randn((c["M"], c["N"]), torch.bfloat16, gen)
+    a, b = shard_range(c["M"], rank, ws) if strong else (0, c["M"])
+    x = _randn((b - a, c["N"]), torch.bfloat16, gen)
+    r = _randn((b - a, c["N"]), torch.bfloat16, gen)
     w = (1 + 0.02 * torch.randn(c["N"], device="cuda", generator=gen)).to(torch.bfloat16)
-    nbytes = rmsnorm_bytes(c["M"], c["N"], 2)
+    job_bytes = rmsnorm_bytes(c["M"], c["N"], 2) * (1 if strong else ws)
     total_ms, per = time_cuda(lambda: fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, ws)
     ms = total_ms / steps
-    return {"ms": ms, "bytes": nbytes, "value": ws * nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "kernel_ms": statistics.mean(per), "launches_per_step": 1}
+    check_device_errors("rmsnorm")
+    return {"ms": ms, "bytes": job_bytes, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "kernel_ms": statistics.mean(per), "launches_per_step": 1, "rows_per_rank": b - a}
 
 
-def bench_serving(ws, rank, max_tokens=64):
+def _prompt_set(cfg, rank, ws, strong):
+    """Config 5's prompt set: 64 lengths U[512, 4096] and token ids U[0, 32000)
+    from seed 0. Strong scaling: this rank's contiguous share of the 64
+    sequences; weak: a full set of its own (seed = rank)."""
+    from lightserve_b200.sharding import shard_range
+
+    c = DEC_CFG
+    g = torch.Generator().manual_seed(0 if strong else rank)
+    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    a, b = shard_range(c["S"], rank, ws) if strong else (0, c["S"])
+    return prompts[a:b]
+
+
+def bench_serving(ws, rank, strong=True, max_tokens=64):
     """Continuous batching end to end (ServingEngine: scheduler, packed
     prefill, CUDA-graph paged decode, host-side token handling each step) on
-    config 5's model and prompt set: all 64 requests submitted at once, each
-    generating max_tokens tokens. Timed on the host around run(), after one
-    warm-up run of the same requests."""
+    config 5's model and prompt set (this rank's share of it): all requests
+    submitted at once, each generating max_tokens tokens. Timed on the host
+    around run(), after one warm-up run of the same requests."""
     from lightserve_b200.engine import CacheConfig, Request, SamplingParams, SchedulerConfig
     from lightserve_b200.model.minimal_llama import decode_bench_config, init_weights
     from lightserve_b200.model.serving import ServingEngine
@@ -270,13 +323,12 @@ def bench_serving(ws, rank, max_tokens=64):
     c = DEC_CFG
     cfg = decode_bench_config()
     w = init_weights(cfg, device="cuda", seed=0)
-    g = torch.Generator().manual_seed(rank)
-    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
-    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    prompts = _prompt_set(cfg, rank, ws, strong)
+    lens = [len(p) for p in prompts]
     bs = c["block_size"]
     blocks = sum(-(-(n + max_tokens) // bs) for n in lens) + 8
     eng = ServingEngine(w, cfg, CacheConfig(block_size=bs, num_gpu_blocks=blocks),
-                        SchedulerConfig(max_num_seqs=c["S"], max_num_batched_tokens=sum(lens)))
+                        SchedulerConfig(max_num_seqs=len(prompts), max_num_batched_tokens=sum(lens)))
     times = []
     for it in range(2):
         for i, p in enumerate(prompts):
@@ -287,24 +339,26 @@ def bench_serving(ws, rank, max_tokens=64):
         out = eng.run()
         torch.cuda.synchronize()
         times.append(time.perf_counter() - t0)
-        assert len(out) == c["S"] and all(len(v) == max_tokens for v in out.values())
+        assert len(out) == len(prompts) and all(len(v) == max_tokens for v in out.values())
     el = max_over_ranks(times[-1], ws)
-    gen = c["S"] * max_tokens
-    return {"seconds": el, "requests": c["S"], "prompt_tokens": sum(lens), "generated_tokens": gen,
-            "value": ws * gen / el, "unit": "generated tokens/s",
-            "total_tokens_per_s": ws * (gen + sum(lens)) / el,
+    mult = 1 if strong else ws
+    n_req = c["S"] * mult
+    gen = n_req * max_tokens
+    total_prompt = _sum_over_ranks(sum(lens), ws)
+    return {"seconds": el, "requests": n_req, "prompt_tokens": total_prompt, "generated_tokens": gen,
+            "value": gen / el, "unit": "generated tokens/s",
+            "total_tokens_per_s": (gen + total_prompt) / el,
             "note": "host-timed ServingEngine.run(): prefill of every prompt, then decode steps"}
 
 
-def bench_varlen(steps, warmup, ws, rank):
-    """Packed (variable-length) causal attention over config 5's prompt set:
-    64 sequences with lengths U[512, 4096], 16 heads x 128, bf16 -- one
+def bench_varlen(steps, warmup, ws, rank, strong=True):
+    """Packed (variable-length) causal attention over config 5's prompt set
+    (this rank's share): lengths U[512, 4096], 16 heads x 128, bf16 -- one
     layer's prefill attention."""
     from lightserve_b200.kernels import flash_attention_varlen
+    from lightserve_b200.model.minimal_llama import decode_bench_config
 
-    c = DEC_CFG
-    g = torch.Generator().manual_seed(rank)
-    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
+    lens = [len(p) for p in _prompt_set(decode_bench_config(), rank, ws, strong)]
     T, H, D = sum(lens), 16, 128
     gen = torch.Generator(device="cuda").manual_seed(2000 + rank)
     q, k, v = (_randn((T, H, D), torch.bfloat16, gen) for _ in range(3))
@@ -313,12 +367,13 @@ def bench_varlen(steps, warmup, ws, rank):
     total_ms, _ = time_cuda(lambda: flash_attention_varlen(q, k, v, cu, max(lens), causal=True, out=out),
                             steps, warmup, ws)
     ms = total_ms / steps
-    flops = sum(attn_fwd_flops(1, H, n, D, True) for n in lens)
-    return {"ms": ms, "flops": flops, "tokens": T, "value": ws * flops / (ms * 1e-3) / 1e12,
-            "unit": "TFLOP/s", "launches_per_step": 1}
+    flops = _sum_over_ranks(sum(attn_fwd_flops(1, H, n, D, True) for n in lens), ws)
+    check_device_errors("varlen attention")
+    return {"ms": ms, "flops": flops, "tokens": _sum_over_ranks(T, ws),
+            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "launches_per_step": 1}
 
 
-def bench_decode(steps, warmup, ws, rank):
+def bench_decode(steps, warmup, ws, rank, strong=True):
     from lightserve_b200.engine import BlockManager, Request
     from lightserve_b200.model.minimal_llama import decode_bench_config, init_weights
     from lightserve_b200.model.paged_decode import PagedDecoder, PagedKVCache
@@ -326,15 +381,15 @@ def bench_decode(steps, warmup, ws, rank):
     c = DEC_CFG
     cfg = decode_bench_config()
     w = init_weights(cfg, device="cuda", seed=0)
-    g = torch.Generator().manual_seed(rank)
-    lens = torch.randint(c["ctx_lo"], c["ctx_hi"] + 1, (c["S"],), generator=g).tolist()
-    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    prompts = _prompt_set(cfg, rank, ws, strong)
+    lens = [len(p) for p in prompts]
+    S = len(prompts)
     bs = c["block_size"]
     max_blocks = -(-(c["ctx_hi"] + c["steps"] + warmup + 2) // bs)
     num_blocks = sum(-(-(n + c["steps"] + warmup + 2) // bs) for n in lens) + 8
     cache = PagedKVCache(cfg, num_blocks, bs)
     bm = BlockManager(block_size=bs, num_gpu_blocks=num_blocks)
-    dec = PagedDecoder(w, cfg, cache, bm, max_batch=c["S"], max_blocks_per_seq=max_blocks)
+    dec = PagedDecoder(w, cfg, cache, bm, max_batch=S, max_blocks_per_seq=max_blocks)
     reqs = [Request(f"r{i}", p) for i, p in enumerate(prompts)]
     dec.admit(reqs, c["steps"] + warmup + 1)
     # Packed prefill of all prompts (already run once by admit), timed again
@@ -342,28 +397,38 @@ def bench_decode(steps, warmup, ws, rank):
     tables = [bm.get_block_table(r) for r in reqs]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    barrier(ws)
     e0.record()
     dec.prefill_packed(reqs, tables)
     e1.record()
     torch.cuda.synchronize()
-    prefill_ms = e0.elapsed_time(e1)
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1), ws)
     dec.capture()
     torch.cuda.nvtx.range_push("decode_steps")  # lets ncu select the timed replays
     total_ms, _ = time_cuda(dec.graph.replay, steps, warmup, ws)
     torch.cuda.nvtx.range_pop()
     ms = total_ms / steps
-    ctx = sum(lens) / len(lens) + warmup + steps / 2
+    check_device_errors("paged decode")
+    mult = 1 if strong else ws
+    n_seq = c["S"] * mult
+    # HBM bytes per step over the whole job: every rank streams the weights
+    # once and its own sequences' K/V.
+    ctx_sum = _sum_over_ranks(sum(lens) + S * (warmup + steps / 2), ws)
     layers = cfg.n_layers
-    kv_bytes = c["S"] * ctx * layers * 2 * cfg.hidden_size * 2
+    kv_bytes = ctx_sum * layers * 2 * cfg.hidden_size * 2
     w_bytes = sum(t.numel() * t.element_size() for t in
                   [w.lm_head] + [getattr(l, n) for l in w.layers for n in
                                  ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")])
-    return {"ms_per_step": ms, "value": ws * c["S"] / (ms * 1e-3), "unit": "tokens/s",
-            "hbm_bytes_per_step": kv_bytes + w_bytes, "achieved_gbs": (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9,
-            "seqs_per_gpu": c["S"], "mean_prompt": sum(lens) / len(lens),
-            "prefill": {"ms": prefill_ms, "tokens": sum(lens),
-                        "tokens_per_s": sum(lens) / (prefill_ms * 1e-3),
-                        "note": "packed prefill of the 64 prompts (varlen attention), CUDA-event timed outside the decode steps"}}
+    job_bytes = kv_bytes + ws * w_bytes
+    total_prompt = _sum_over_ranks(sum(lens), ws)
+    return {"ms_per_step": ms, "value": n_seq / (ms * 1e-3), "unit": "tokens/s",
+            "hbm_bytes_per_step": job_bytes, "achieved_gbs": job_bytes / (ms * 1e-3) / 1e9,
+            "achieved_gbs_per_gpu": job_bytes / ws / (ms * 1e-3) / 1e9,
+            "seqs_per_gpu": S, "mean_prompt": total_prompt / n_seq,
+            "prefill": {"ms": prefill_ms, "tokens": total_prompt,
+                        "tokens_per_s": total_prompt / (prefill_ms * 1e-3),
+                        "note": "packed prefill of every prompt (varlen attention), CUDA-event timed "
+                                "outside the decode steps, max over ranks"}}
 
 
 def bench_torch_sdpa(steps, warmup):
@@ -392,57 +457,183 @@ def bench_torch_sdpa(steps, warmup):
 
 
 # ------------------------------------------------------------- CPU baseline --
-def cpu_attention_sample(target_s: float = 10.0):
-    """The reference's CPU path for config 2 (dense fp32 causal attention, the
-    oracle in oracle/attention.py) on a bounded sample of (b, h) slices of the
-    same shape, all host threads. Returns (TFLOP/s, cores, sample text)."""
-    from oracle.attention import attention_ref, attn_fwd_flops
-
+def _cpu_threads():
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
+    return cores
+
+
+def _sdpa_cpu(q, k, v):
+    """lightserve's CPU comparison path for attention: PyTorch SDPA, causal,
+    implicit 1/sqrt(D) scale (kernels/tests/test_flash_attention.py:47)."""
+    import torch.nn.functional as F
+
+    return F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+
+def cpu_attention_sample(target_s: float = 8.0):
+    """Config 2 on the host cores through the reference's CPU path (fp32 SDPA)
+    over as many (b, h) slices of the config's shape as fit in ~target_s.
+    Returns (TFLOP/s, cores, sample text)."""
+    cores = _cpu_threads()
     c = FWD_CFG
     g = torch.Generator().manual_seed(0)
-    q, k, v = (torch.randn(1, 1, c["N"], c["D"], generator=g) for _ in range(3))
-    slices, t0 = 0, time.perf_counter()
-    while True:
-        attention_ref(q, k, v, True)
-        slices += 1
-        el = time.perf_counter() - t0
-        if el >= target_s or slices >= c["B"] * c["H"]:
-            break
+    q, k, v = (torch.randn(1, 4, c["N"], c["D"], generator=g) for _ in range(3))
+    with torch.no_grad():
+        _sdpa_cpu(q, k, v)  # warm-up
+        slices, t0 = 0, time.perf_counter()
+        while True:
+            _sdpa_cpu(q, k, v)
+            slices += 4
+            el = time.perf_counter() - t0
+            if el >= target_s or slices >= c["B"] * c["H"]:
+                break
     flops = attn_fwd_flops(1, slices, c["N"], c["D"], True)
-    return flops / el / 1e12, cores, (f"{slices} of {c['B'] * c['H']} (b,h) slices of N={c['N']} D={c['D']} "
-                                      f"causal, fp32 dense softmax(QK^T)V, {el:.1f} s")
+    return flops / el / 1e12, cores, (f"{slices} of {c['B'] * c['H']} (b,h) slices of N={c['N']} "
+                                      f"D={c['D']} causal, fp32 torch SDPA on the host, {el:.1f} s")
+
+
+def cpu_backward_sample(target_s: float = 5.0):
+    """Config 3 on the host: SDPA autograd fp32 (the reference's gradient
+    oracle, kernels/tests/test_flash_attention_backward.py:69-90), backward
+    only timed, over (b, h) slices of the config's shape."""
+    cores = _cpu_threads()
+    c = BWD_CFG
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, 4, c["N"], c["D"], generator=g).requires_grad_() for _ in range(3))
+    do = torch.randn(1, 4, c["N"], c["D"], generator=g)
+    slices, el = 0, 0.0
+    while el < target_s and slices < c["B"] * c["H"]:
+        o = _sdpa_cpu(q, k, v)
+        t0 = time.perf_counter()
+        torch.autograd.grad(o, (q, k, v), do)
+        el += time.perf_counter() - t0
+        slices += 4
+    flops = attn_bwd_flops(1, slices, c["N"], c["D"], True)
+    return {"value": flops / el / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+            "sample": f"{slices} of {c['B'] * c['H']} (b,h) slices, fp32 SDPA autograd backward on the "
+                      f"host, {el:.1f} s"}
+
+
+def cpu_rmsnorm_sample(target_s: float = 3.0):
+    """Config 4 on the host: lightserve's eager add+RMSNorm
+    (rmsnorm_residual_reference, kernels/tests/test_fused_rmsnorm_residual.py:24-29)
+    in fp32 over row blocks of the config; GB/s counts the config's bf16
+    bytes for the rows processed (same work as the GPU line)."""
+    from oracle.rmsnorm import rmsnorm_residual
+
+    cores = _cpu_threads()
+    c = RMS_CFG
+    g = torch.Generator().manual_seed(0)
+    rows = 1024
+    x, r = (torch.randn(rows, c["N"], generator=g) for _ in range(2))
+    w = 1 + 0.02 * torch.randn(c["N"], generator=g)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        rmsnorm_residual(x, r, w, 1e-6)
+        done += rows
+        el = time.perf_counter() - t0
+        if el >= target_s or done >= c["M"]:
+            break
+    return {"value": rmsnorm_bytes(done, c["N"], 2) / el / 1e9, "unit": "GB/s", "cores": cores,
+            "kind": "port", "sample": f"{done} of {c['M']} rows, fp32 eager add+RMSNorm, {el:.1f} s"}
+
+
+def cpu_decode_sample(steps: int = 2):
+    """Config 5 on the host: lightserve's decode is a full recompute of
+    reference_llama_forward per step (model/cuda_graph_decode.py:108-118);
+    this times `steps` greedy steps of ONE sequence at the prompt set's mean
+    length in fp32 and extrapolates tokens/s for the batch of 64 as 64
+    sequences at that per-sequence rate run one after another (the forward is
+    compute-bound on the host, so batching does not change the total)."""
+    from lightserve_b200.model.minimal_llama import decode_bench_config, init_weights
+    from oracle.llama import reference_forward
+
+    cores = _cpu_threads()
+    cfg = decode_bench_config(dtype=torch.float32)
+    w = init_weights(cfg, device="cpu", seed=0)
+    g = torch.Generator().manual_seed(0)
+    n = 2400
+    ids = torch.randint(0, cfg.vocab_size, (1, n), generator=g)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(steps):
+            nxt = reference_forward(w, cfg, ids)[0, -1].argmax().view(1, 1)
+            ids = torch.cat([ids, nxt], dim=1)
+    el = time.perf_counter() - t0
+    return {"value": steps / el, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "extrapolated": True,
+            "sample": f"{steps} full-recompute greedy steps of 1 sequence at {n} tokens, fp32, "
+                      f"{el:.1f} s; the batch of {DEC_CFG['S']} is extrapolated at this per-sequence rate"}
+
+
+def bench_reference_triton(steps, warmup):
+    """Context, not the product: lightserve's own Triton kernels (staged
+    unmodified under baseline/_ref by tests/stage_reference_kernels.py) on
+    configs 2, 3 and 4 on this GPU, same FLOP/byte conventions."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "kernels" / "flash_attention.py").exists():
+        return {"unavailable": "reference kernels not staged (tests/stage_reference_kernels.py)"}
+    sys.path.insert(0, str(ref))
+    try:
+        from kernels import flash_attention as rfa
+        from kernels import flash_attention_backward as rfb
+        from kernels import fused_rmsnorm_residual as rrn
+    finally:
+        sys.path.remove(str(ref))
+    out = {}
+    gen = torch.Generator(device="cuda").manual_seed(4000)
+    c = FWD_CFG
+    q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(3))
+    total, _ = time_cuda(lambda: rfa.flash_attention_forward(q, k, v, causal=True), steps, warmup, 1)
+    out["fwd_tflops"] = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
+    del q, k, v
+    c = BWD_CFG
+    q, k, v, do = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(4))
+    o, L = rfb._flash_attention_forward_lse(q, k, v, True)
+    total, _ = time_cuda(lambda: rfb._flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, 1)
+    out["bwd_tflops"] = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
+    del q, k, v, do, o, L
+    c = RMS_CFG
+    x, r = (_randn((c["M"], c["N"]), torch.bfloat16, gen) for _ in range(2))
+    w = (1 + 0.02 * torch.randn(c["N"], device="cuda", generator=gen)).to(torch.bfloat16)
+    total, _ = time_cuda(lambda: rrn.fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, 1)
+    out["rmsnorm_gbs"] = rmsnorm_bytes(c["M"], c["N"], 2) / (total / steps * 1e-3) / 1e9
+    out["note"] = "lightserve's Triton kernels (JIT for sm_100 by Triton) on this GPU; context only"
+    return out
 
 
 def run_reference(args, rank, ws):
-    """--impl reference: the reference's CPU implementation of the path (the
-    oracle port: lightserve's GPU code is Triton and its CPU path is PyTorch
-    SDPA), timed on this host on config 2's metric. Rank 0 only."""
+    """--impl reference: the reference's CPU implementation of the path,
+    PyTorch SDPA in fp32 (lightserve's own comparison target,
+    kernels/tests/test_flash_attention.py:47; its GPU code is Triton), on
+    this host's cores, on config 2's metric. Each step is a bounded sample
+    of 8 (b, h) slices of config 2. Rank 0 only."""
     if rank != 0:
         return
-    from oracle.attention import attention_ref, attn_fwd_flops
-
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
+    cores = _cpu_threads()
     c = FWD_CFG
     g = torch.Generator().manual_seed(0)
-    q, k, v = (torch.randn(1, 1, c["N"], c["D"], generator=g) for _ in range(3))
-    for _ in range(max(args.warmup, 1)):
-        attention_ref(q, k, v, True)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        attention_ref(q, k, v, True)
-    el = time.perf_counter() - t0
-    flops = attn_fwd_flops(1, args.steps, c["N"], c["D"], True)
+    per_step = 8
+    q, k, v = (torch.randn(1, per_step, c["N"], c["D"], generator=g) for _ in range(3))
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 1)):
+            _sdpa_cpu(q, k, v)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _sdpa_cpu(q, k, v)
+        el = time.perf_counter() - t0
+    flops = attn_fwd_flops(1, per_step * args.steps, c["N"], c["D"], True)
     val = flops / el / 1e12
-    sample = f"1 (b,h) slice of config 2 per step (N={c['N']} D={c['D']} causal fp32)"
+    sample = (f"{per_step} (b,h) slices of config 2 per step (N={c['N']} D={c['D']} causal), "
+              f"fp32 torch SDPA on {cores} host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": CONFIG,
-        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+                         "sample": sample},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -458,56 +649,75 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--only", default="fwd,bwd,rmsnorm,varlen,decode,serving,context",
+    ap.add_argument("--only", default="fwd,bwd,rmsnorm,varlen,decode,serving,context,triton",
                     help="comma list of workloads (fwd is always run: it is the headline)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--strong", action="store_true",
-                    help="split config 2's (b,h) slices across ranks instead of one full config per rank")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: each configuration's fixed work is split across the ranks; "
+                         "weak: every rank runs a full configuration")
     args = ap.parse_args()
     rank, ws, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, rank, ws)
         return
     args.warmup = max(args.warmup, 3)
+    strong = args.scaling == "strong"
     peaks = load_peaks()
     traffic = load_traffic()
     only = set(args.only.split(","))
     with ClockSampler(local) as clk:
         fwd = bench_fwd(args.steps, args.warmup, ws, rank, peaks, e2e_steps=min(args.steps, 5),
-                        strong=args.strong)
+                        strong=strong)
     secondary = {}
     if "bwd" in only:
-        secondary["fa_bwd"] = bench_bwd(args.steps, args.warmup, ws, rank)
+        secondary["fa_bwd"] = bench_bwd(args.steps, args.warmup, ws, rank, strong)
         secondary["fa_bwd"]["frac_of_peak"] = secondary["fa_bwd"]["value"] / ws / peaks["bf16_tflops"]
     if "rmsnorm" in only:
-        secondary["rmsnorm"] = bench_rmsnorm(args.steps, args.warmup, ws, rank)
+        secondary["rmsnorm"] = bench_rmsnorm(args.steps, args.warmup, ws, rank, strong)
         secondary["rmsnorm"]["frac_of_peak"] = secondary["rmsnorm"]["value"] / ws / peaks["hbm_gbs"]
     if "varlen" in only:
-        secondary["varlen_prefill_attn"] = bench_varlen(args.steps, args.warmup, ws, rank)
+        secondary["varlen_prefill_attn"] = bench_varlen(args.steps, args.warmup, ws, rank, strong)
         secondary["varlen_prefill_attn"]["frac_of_peak"] = (secondary["varlen_prefill_attn"]["value"] / ws
                                                              / peaks["bf16_tflops"])
     if "decode" in only:
-        secondary["paged_decode"] = bench_decode(min(args.steps * 4, 128), args.warmup, ws, rank)
+        secondary["paged_decode"] = bench_decode(min(args.steps * 4, 128), args.warmup, ws, rank, strong)
+        secondary["paged_decode"]["frac_of_peak"] = (secondary["paged_decode"]["achieved_gbs_per_gpu"]
+                                                     / peaks["hbm_gbs"])
     if "serving" in only:
-        secondary["serving"] = bench_serving(ws, rank)
+        secondary["serving"] = bench_serving(ws, rank, strong)
     if ws == 1 and "context" in only:
         try:
             secondary["torch_sdpa_context"] = bench_torch_sdpa(args.steps, args.warmup)
         except Exception as e:  # context only: never fail the bench on it
             secondary["torch_sdpa_context"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    if ws == 1 and "triton" in only:
+        try:
+            secondary["reference_triton_context"] = bench_reference_triton(args.steps, args.warmup)
+        except Exception as e:  # context only: never fail the bench on it
+            secondary["reference_triton_context"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     if rank != 0:
         return
     cpu = None
     if not args.no_cpu_baseline:
         v, cores, sample = cpu_attention_sample()
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "reference", "sample": sample}
+        if ws == 1:
+            if "bwd" in secondary:
+                secondary["fa_bwd"]["cpu_baseline"] = cpu_backward_sample()
+            if "rmsnorm" in secondary:
+                secondary["rmsnorm"]["cpu_baseline"] = cpu_rmsnorm_sample()
+            if "paged_decode" in secondary:
+                secondary["paged_decode"]["cpu_baseline"] = cpu_decode_sample()
     achieved = fwd["kernel_tflops"]
     tr = traffic.get("attn_fwd", {}).get("dram_bytes_per_launch")
+    config = dict(CONFIG)
+    config["parallelism"] = (f"(b,h) slices split over {ws} GPU(s), {fwd['slices_per_rank']} per rank"
+                             if strong else f"{ws} replica(s) of the full config")
     line = {
         "metric": METRIC, "value": fwd["value"], "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": fwd["ms"], "higher_is_better": True,
-        "scaling": "strong" if args.strong else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))", "config": CONFIG,
+        "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))", "config": config,
         "e2e": {k: v for k, v in fwd["e2e"].items() if k != "steps"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": tr,
@@ -515,6 +725,7 @@ def main():
         "cpu_baseline": cpu,
         "gpu_launches": fwd["launches_per_step"] * args.steps,
         "clocks": clk.summary(),
+        "device_errors": DEVICE_ERRORS,
         "secondary": secondary,
     }
     print(json.dumps(line))
