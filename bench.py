@@ -172,22 +172,29 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def time_cuda(fn, steps: int, warmup: int, ws: int):
+def time_cuda(fn, steps: int, warmup: int, ws: int, per_call: bool = True):
     """Warm-up, then EXACTLY `steps` calls bracketed by barrier + synchronize;
-    returns (max-over-ranks total ms, per-call event ms list)."""
+    returns (max-over-ranks total ms, per-call event ms list). With
+    per_call=False only the two bracketing events are recorded (no event
+    records between the calls); the list is then empty."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps if per_call else 0)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(s)
-    for a, b in evs:
-        a.record(s)
-        fn()
-        b.record(s)
+    if per_call:
+        for a, b in evs:
+            a.record(s)
+            fn()
+            b.record(s)
+    else:
+        for _ in range(steps):
+            fn()
     t1.record(s)
     torch.cuda.synchronize()
     barrier(ws)
@@ -271,7 +278,8 @@ def bench_bwd(steps, warmup, ws, rank, strong=True):
     q, k, v, do = (_randn(shape, torch.bfloat16, gen) for _ in range(4))
     o, L = _flash_attention_forward_lse(q, k, v, True)
     job_flops = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) * (1 if strong else ws)
-    total_ms, per = time_cuda(lambda: _flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, ws)
+    total_ms, _ = time_cuda(lambda: _flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, ws,
+                            per_call=False)
     ms = total_ms / steps
     check_device_errors("attention backward")
     return {"ms": ms, "flops": job_flops, "value": job_flops / (ms * 1e-3) / 1e12,
@@ -289,11 +297,11 @@ def bench_rmsnorm(steps, warmup, ws, rank, strong=True):
     r = _randn((b - a, c["N"]), torch.bfloat16, gen)
     w = (1 + 0.02 * torch.randn(c["N"], device="cuda", generator=gen)).to(torch.bfloat16)
     job_bytes = rmsnorm_bytes(c["M"], c["N"], 2) * (1 if strong else ws)
-    total_ms, per = time_cuda(lambda: fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, ws)
+    total_ms, _ = time_cuda(lambda: fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, ws, per_call=False)
     ms = total_ms / steps
     check_device_errors("rmsnorm")
     return {"ms": ms, "bytes": job_bytes, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "kernel_ms": statistics.mean(per), "launches_per_step": 1, "rows_per_rank": b - a}
+            "launches_per_step": 1, "rows_per_rank": b - a}
 
 
 def _prompt_set(cfg, rank, ws, strong):
@@ -365,7 +373,7 @@ def bench_varlen(steps, warmup, ws, rank, strong=True):
     cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
     total_ms, _ = time_cuda(lambda: flash_attention_varlen(q, k, v, cu, max(lens), causal=True, out=out),
-                            steps, warmup, ws)
+                            steps, warmup, ws, per_call=False)
     ms = total_ms / steps
     flops = _sum_over_ranks(sum(attn_fwd_flops(1, H, n, D, True) for n in lens), ws)
     check_device_errors("varlen attention")
@@ -441,7 +449,7 @@ def bench_torch_sdpa(steps, warmup):
     c = FWD_CFG
     q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(3))
     with torch.no_grad():
-        total, _ = time_cuda(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), steps, warmup, 1)
+        total, _ = time_cuda(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), steps, warmup, 1, False)
     fwd = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
     del q, k, v
     c = BWD_CFG
@@ -450,7 +458,7 @@ def bench_torch_sdpa(steps, warmup):
     do = _randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen)
     o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
     total, _ = time_cuda(lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True),
-                         steps, warmup, 1)
+                         steps, warmup, 1, False)
     bwd = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
     return {"fwd_tflops": fwd, "bwd_tflops": bwd,
             "note": "torch.nn.functional.scaled_dot_product_attention, bf16, causal; context only"}
@@ -585,19 +593,19 @@ def bench_reference_triton(steps, warmup):
     gen = torch.Generator(device="cuda").manual_seed(4000)
     c = FWD_CFG
     q, k, v = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(3))
-    total, _ = time_cuda(lambda: rfa.flash_attention_forward(q, k, v, causal=True), steps, warmup, 1)
+    total, _ = time_cuda(lambda: rfa.flash_attention_forward(q, k, v, causal=True), steps, warmup, 1, False)
     out["fwd_tflops"] = attn_fwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
     del q, k, v
     c = BWD_CFG
     q, k, v, do = (_randn((c["B"], c["H"], c["N"], c["D"]), torch.bfloat16, gen) for _ in range(4))
     o, L = rfb._flash_attention_forward_lse(q, k, v, True)
-    total, _ = time_cuda(lambda: rfb._flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, 1)
+    total, _ = time_cuda(lambda: rfb._flash_attention_backward(do, q, k, v, o, L, True), steps, warmup, 1, False)
     out["bwd_tflops"] = attn_bwd_flops(c["B"], c["H"], c["N"], c["D"], True) / (total / steps * 1e-3) / 1e12
     del q, k, v, do, o, L
     c = RMS_CFG
     x, r = (_randn((c["M"], c["N"]), torch.bfloat16, gen) for _ in range(2))
     w = (1 + 0.02 * torch.randn(c["N"], device="cuda", generator=gen)).to(torch.bfloat16)
-    total, _ = time_cuda(lambda: rrn.fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, 1)
+    total, _ = time_cuda(lambda: rrn.fused_add_rmsnorm(x, r, w, 1e-6), steps, warmup, 1, False)
     out["rmsnorm_gbs"] = rmsnorm_bytes(c["M"], c["N"], 2) / (total / steps * 1e-3) / 1e9
     out["note"] = "lightserve's Triton kernels (JIT for sm_100 by Triton) on this GPU; context only"
     return out

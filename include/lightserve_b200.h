@@ -230,6 +230,30 @@ LSB_API int lsb_swiglu(const void* gu, void* out, int64_t S, int64_t I, int64_t 
                        int64_t ld_out, int dtype, void* stream);
 
 /*
+ * Weight-streaming linear layer for decode batches: y[S, N] = x[S, K] @ W[K, N]
+ * with fp32 accumulation and one rounding to dtype (bf16 or fp16).
+ * Replaces the projections of lightserve's decode step, `h @ w` in
+ * model/minimal_llama.py:216-234 (q/k/v, o, gate/up, down) and :249
+ * (lm_head), which lightserve runs through torch.matmul / its Triton
+ * kernels/tiled_matmul.py:55-151.
+ * The weight is packed once with lsb_linear_pack from W^T ([N, K], row
+ * stride ldw, K contiguous) into lsb_linear_packed_bytes(N, K) bytes of
+ * 16 KiB tiles (128 features x 64 of K, 128-byte swizzled, zero-padded).
+ * x is [S, K] (row stride ldx), y is [S, N] (row stride ldy).
+ * Limits: 1 <= S <= 128; K a multiple of 8; x and the packed weight 16-byte
+ * aligned, ldx a multiple of 8. Needs no scratch memory; the result does not
+ * depend on timing (fixed summation order).
+ * pdl != 0 launches with programmatic stream serialisation: the weight
+ * stream may start while the previous kernel of the stream finishes (x is
+ * read only after that kernel has completed).
+ */
+LSB_API int64_t lsb_linear_packed_bytes(int64_t N, int64_t K);
+LSB_API int lsb_linear_pack(const void* w_t, int64_t ldw, int64_t N, int64_t K, int dtype,
+                            void* packed, int64_t packed_bytes, void* stream);
+LSB_API int lsb_linear(const void* x, int64_t ldx, const void* w_packed, void* y, int64_t ldy,
+                       int64_t S, int64_t N, int64_t K, int dtype, int pdl, void* stream);
+
+/*
  * Allocation-free paged decode. No counterpart exists in lightserve: this is
  * lsb_paged_decode for callers that cannot allocate device memory (runtimes
  * whose own pool owns the GPU's memory, FFI bindings without access to the

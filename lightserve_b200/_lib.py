@@ -64,6 +64,9 @@ SIGNATURES = {
     "lsb_rope_kv_write_slots": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
                                      _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_swiglu": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lsb_linear_packed_bytes": (_I64, [_I64, _I64]),
+    "lsb_linear_pack": (_I, [_P, _I64, _I64, _I64, _I, _P, _I64, _P]),
+    "lsb_linear": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P]),
     "lsb_paged_decode_static_scratch_capacity": (_I64, []),
     "lsb_paged_decode_static_scratch": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                              _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),

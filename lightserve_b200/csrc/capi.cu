@@ -56,6 +56,7 @@ int attn_fwd_tc_device_error(bool reset);
 int attn_bwd_tc_device_error(bool reset);
 int paged_decode_device_error(bool reset);
 int selftest_device_error(bool reset);
+int linear_device_error(bool reset);
 
 
 }  // namespace lsb
@@ -65,7 +66,8 @@ extern "C" const char* lsb_last_error(void) { return lsb::g_err; }
 static int device_error_all(bool reset) {
   int e = 0;
   for (int v : {lsb::attn_fwd_tc_device_error(reset), lsb::attn_bwd_tc_device_error(reset),
-                lsb::paged_decode_device_error(reset), lsb::selftest_device_error(reset)})
+                lsb::paged_decode_device_error(reset), lsb::selftest_device_error(reset),
+                lsb::linear_device_error(reset)})
     if (!e) e = v;
   if (e == LSB_DEVICE_ERR_QUERY)
     lsb::set_error("device error words unreadable: %s", cudaGetErrorString(cudaGetLastError()));

@@ -200,6 +200,13 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Lets the next kernel of the stream, when it was launched with programmatic
+// stream serialisation, start before this one finishes (it still waits for
+// this kernel's completion before reading its results). No effect otherwise.
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Workspace regions are padded to 256 bytes.

@@ -189,6 +189,7 @@ paged_decode_combine_kernel(const int32_t* __restrict__ context_lens, int max_to
                             T* __restrict__ o, int H, int64_t so_s, int64_t so_h, int max_parts,
                             const float* __restrict__ part_m, const float* __restrict__ part_l,
                             const float* __restrict__ part_acc) {
+  allow_dependents();
   const int h = blockIdx.x, s = blockIdx.y;
   const int ctx = max(0, min(context_lens[s], max_tokens));
   const int nparts = (ctx + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
@@ -226,6 +227,7 @@ paged_decode_bulk_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
                          int max_blocks, int num_blocks, int64_t sq_s, int64_t sq_h, int64_t so_s,
                          int64_t so_h, float scale_log2, int max_parts, float* __restrict__ part_m,
                          float* __restrict__ part_l, float* __restrict__ part_acc) {
+  allow_dependents();
   using namespace sm100;
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LPT = D / VEC;                    // lanes per token row

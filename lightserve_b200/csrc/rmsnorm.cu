@@ -22,6 +22,7 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
                             const T* __restrict__ w, T* __restrict__ out,
                             T* __restrict__ h_out, int N, int64_t ld_x,
                             int64_t ld_r, int64_t ld_o, int64_t ld_h, float eps) {
+  allow_dependents();
   constexpr int VEC = Vec16<T>::N;
   const int row = blockIdx.x;
   const int nvec = N / VEC;

@@ -25,6 +25,7 @@ __device__ __forceinline__ T silu_mul(T g, T u) {
 template <typename T>
 __global__ void swiglu_vec_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t S,
                                   int64_t I, int64_t ld_gu, int64_t ld_out) {
+  allow_dependents();
   constexpr int VEC = Vec16<T>::N;
   const int64_t nv = I / VEC;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < S * nv;

@@ -10,11 +10,15 @@ side-stream warm-up before capture (``:129-135``), one captured step
 (``:137-139``), replay per token, greedy ``argmax`` of the newest position's
 logits (``:114-118``).
 
-Per step and layer: fused add+RMSNorm (lsb kernel) -> fused QKV GEMM (cuBLAS)
+Per step and layer: fused add+RMSNorm (lsb kernel) -> fused QKV projection
 -> ``rope_kv_write`` (lsb kernel: RoPE at each sequence's position, K/V into
 the cache slot from the block table, context lengths) ->
 ``paged_decode_attention`` (lsb kernel) -> O projection -> add+RMSNorm ->
-SwiGLU MLP. All buffers are static, so a step is graph-capturable.
+fused gate|up projection -> SwiGLU (lsb kernel) -> down projection; then the
+final norm and the lm_head projection. The projections run on cuBLAS, or
+with ``use_lsb_linear`` (bf16/fp16, at most 128 sequences) on
+``lsb_linear`` (tcgen05 weight streaming). All buffers are static, so a step
+is graph-capturable.
 
 Prefill: with a bf16/fp16 model and head_dim 64 or 128, every admitted prompt
 runs in ONE packed forward ([sum of prompt lengths, hidden]: the GEMMs see
@@ -39,6 +43,8 @@ from ..engine import BlockManager, Request
 from ..kernels.fused_rmsnorm_residual import fused_add_rmsnorm
 from ..kernels.fused_swiglu import silu_and_mul
 from ..kernels.flash_attention import flash_attention_varlen
+from ..kernels.linear import MAX_ROWS as LINEAR_MAX_ROWS
+from ..kernels.linear import linear, pack_linear_weight
 from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
                                         rope_kv_write, rope_kv_write_slots, write_kv_cache)
 from .minimal_llama import LlamaConfig, LlamaWeights, llama_forward, precompute_rope
@@ -67,8 +73,12 @@ def slots_for_positions(table, positions, block_size: int):
 
 @dataclass
 class _Fused:
-    w_qkv: torch.Tensor
-    w_gu: torch.Tensor
+    """Per-layer projection weights held transposed ([out, in], in contiguous),
+    the layout lsb_linear streams; ``.t()`` views serve the prefill GEMMs."""
+    w_qkv_t: torch.Tensor
+    w_gu_t: torch.Tensor
+    w_o_t: torch.Tensor
+    w_down_t: torch.Tensor
 
 
 class PagedDecoder:
@@ -76,13 +86,27 @@ class PagedDecoder:
 
     def __init__(self, weights: LlamaWeights, config: LlamaConfig, cache: PagedKVCache,
                  block_manager: BlockManager, max_batch: int, max_blocks_per_seq: int,
-                 device="cuda"):
+                 device="cuda", use_lsb_linear: bool = False):
         self.w, self.cfg, self.cache, self.bm = weights, config, cache, block_manager
         self.device = torch.device(device)
         self.S, self.MB = max_batch, max_blocks_per_seq
-        self.fused = [_Fused(torch.cat([l.q_proj, l.k_proj, l.v_proj], dim=1).contiguous(),
-                             torch.cat([l.gate_proj, l.up_proj], dim=1).contiguous())
+        self.fused = [_Fused(torch.cat([l.q_proj, l.k_proj, l.v_proj], dim=1).t().contiguous(),
+                             torch.cat([l.gate_proj, l.up_proj], dim=1).t().contiguous(),
+                             l.o_proj.t().contiguous(), l.down_proj.t().contiguous())
                       for l in weights.layers]
+        self.lm_head_t = weights.lm_head.t().contiguous()
+        # Decode projections on lsb_linear (weights packed once into its tile
+        # layout) when asked for and it serves this model and batch; cuBLAS
+        # otherwise. Off by default: at config 5's shapes cuBLAS is faster
+        # (measured, see the design notes of lsb_linear).
+        self.lsb_linear = (use_lsb_linear and config.dtype in (torch.bfloat16, torch.float16)
+                           and max_batch <= LINEAR_MAX_ROWS)
+        self._packed = {}
+        if self.lsb_linear:
+            for fz in self.fused:
+                for w_t in (fz.w_qkv_t, fz.w_gu_t, fz.w_o_t, fz.w_down_t):
+                    self._packed[id(w_t)] = pack_linear_weight(w_t)
+            self._packed[id(self.lm_head_t)] = pack_linear_weight(self.lm_head_t)
         self.cos, self.sin = precompute_rope(config, self.device)
         S, Hd, H, D = max_batch, config.hidden_size, config.n_heads, config.head_dim
         dev = self.device
@@ -193,14 +217,14 @@ class PagedDecoder:
         for li, layer in enumerate(self.w.layers):
             fz = self.fused[li]
             normed, residual = fused_add_rmsnorm(x, residual, layer.input_layernorm_weight, eps=cfg.rms_eps)
-            qkv = (normed @ fz.w_qkv).view(T, 3, H, D)
+            qkv = (normed @ fz.w_qkv_t.t()).view(T, 3, H, D)
             rope_kv_write_slots(qkv, self.cos, self.sin, positions, slots, q_rot, k_rot,
                                 self.cache.k[li], self.cache.v[li])
             flash_attention_varlen(q_rot, k_rot, qkv[:, 2], cu, max(lens), causal=True, out=attn)
             x = attn.view(T, Hd) @ layer.o_proj
             normed2, residual = fused_add_rmsnorm(x, residual, layer.post_attention_layernorm_weight,
                                                   eps=cfg.rms_eps)
-            x = silu_and_mul(normed2 @ fz.w_gu) @ layer.down_proj
+            x = silu_and_mul(normed2 @ fz.w_gu_t.t()) @ layer.down_proj
         last = (cu[1:] - 1).long()
         final, _ = fused_add_rmsnorm(x[last].contiguous(), residual[last].contiguous(), self.w.norm_weight,
                                      eps=cfg.rms_eps)
@@ -255,6 +279,12 @@ class PagedDecoder:
         return [int(nxt[s_]) for s_ in slots]
 
     # ----------------------------------------------------------------- step --
+    def _proj(self, x: torch.Tensor, w_t: torch.Tensor) -> torch.Tensor:
+        """x @ w for a decode batch, with w held transposed."""
+        if self.lsb_linear:
+            return linear(x, self._packed[id(w_t)])
+        return x @ w_t.t()
+
     def step(self) -> torch.Tensor:
         """One greedy decode step over the static buffers; returns next tokens [S]."""
         cfg, S, bs = self.cfg, self.S, self.cache.block_size
@@ -262,23 +292,24 @@ class PagedDecoder:
         pos = self.positions
         residual = F.embedding(self.tokens, self.w.embed_tokens)
         x = self.zeros
+        mm = self._proj
         for li, layer in enumerate(self.w.layers):
             fz = self.fused[li]
             normed, residual = fused_add_rmsnorm(x, residual, layer.input_layernorm_weight, eps=cfg.rms_eps)
-            qkv = (normed @ fz.w_qkv).view(S, 3, H, D)
+            qkv = mm(normed, fz.w_qkv_t).view(S, 3, H, D)
             # RoPE at each sequence's position + K/V into its cache slot, fused
             # (also sets context_lens = positions + 1).
             q = rope_kv_write(qkv, self.cos, self.sin, pos, self.block_tables, self.q_rot,
                               self.cache.k[li], self.cache.v[li], self.context_lens)
             attn = paged_decode_attention(q, self.cache.k[li], self.cache.v[li], self.block_tables,
                                           self.context_lens, out=self.attn_out, workspace=self.ws)
-            x = attn.view(S, Hd) @ layer.o_proj
+            x = mm(attn.view(S, Hd), fz.w_o_t)
             normed2, residual = fused_add_rmsnorm(x, residual, layer.post_attention_layernorm_weight,
                                                   eps=cfg.rms_eps)
-            gu = normed2 @ fz.w_gu
-            x = silu_and_mul(gu, out=self.act) @ layer.down_proj
+            gu = mm(normed2, fz.w_gu_t)
+            x = mm(silu_and_mul(gu, out=self.act), fz.w_down_t)
         final, _ = fused_add_rmsnorm(x, residual, self.w.norm_weight, eps=cfg.rms_eps)
-        logits = final @ self.w.lm_head
+        logits = mm(final, self.lm_head_t)
         nxt = logits.argmax(-1)
         self.tokens.copy_(nxt)
         self.positions.add_(1)

@@ -16,7 +16,7 @@
   FFN 5632, vocab 32000), 4 sequences with prompts from U[512, 4096], 16
   greedy steps through PagedDecoder.admit (packed tcgen05 prefill in bf16) and
   the CUDA graph: bf16 teacher-forced against the oracle forward run on the GPU
-  in bf16, and fp32 free-running against the full-recompute greedy loop of
+  in bf16 (projections on cuBLAS and on lsb_linear), and fp32 free-running against the full-recompute greedy loop of
   model/cuda_graph_decode.py:108-118 (exact token ids).
 """
 import math
@@ -96,7 +96,7 @@ def test_config3_backward_full_size(B, H, N, causal, samples):
 
 
 # ------------------------------------------------------------------ config 5
-def _config5_decoder(dtype, n_seqs, steps, seed=0):
+def _config5_decoder(dtype, n_seqs, steps, seed=0, use_lsb_linear=False):
     cfg = decode_bench_config(dtype=dtype)
     w = init_weights(cfg, device="cuda", seed=0)
     g = torch.Generator().manual_seed(seed)
@@ -107,13 +107,15 @@ def _config5_decoder(dtype, n_seqs, steps, seed=0):
     cache = PagedKVCache(cfg, num_blocks, bs)
     bm = BlockManager(block_size=bs, num_gpu_blocks=num_blocks)
     dec = PagedDecoder(w, cfg, cache, bm, max_batch=n_seqs,
-                       max_blocks_per_seq=-(-(4096 + steps + 2) // bs))
+                       max_blocks_per_seq=-(-(4096 + steps + 2) // bs), use_lsb_linear=use_lsb_linear)
+    assert dec.lsb_linear == use_lsb_linear
     return cfg, w, prompts, dec
 
 
-def test_config5_bf16_decode_teacher_forced(capsys):
+@pytest.mark.parametrize("use_lsb_linear", [False, True], ids=["cublas_proj", "lsb_linear_proj"])
+def test_config5_bf16_decode_teacher_forced(capsys, use_lsb_linear):
     steps, n = 16, 4
-    cfg, w, prompts, dec = _config5_decoder(torch.bfloat16, n, steps)
+    cfg, w, prompts, dec = _config5_decoder(torch.bfloat16, n, steps, use_lsb_linear=use_lsb_linear)
     assert dec.packed_prefill_supported()
     reqs = [Request(f"r{i}", p) for i, p in enumerate(prompts)]
     out = dec.generate(reqs, steps, use_graph=True)
@@ -136,7 +138,7 @@ def test_config5_bf16_decode_teacher_forced(capsys):
         del logits
     total = n * steps
     with capsys.disabled():
-        print(f"\nconfig-5 bf16 decode: {checked}/{total} steps above margin {BF16_MARGIN} checked "
+        print(f"\nconfig-5 bf16 decode ({'lsb_linear' if use_lsb_linear else 'cuBLAS'} projections): {checked}/{total} steps above margin {BF16_MARGIN} checked "
               f"(min checked margin {min_margin_checked:.4f}); argmax agreement {agree}/{total}")
     assert checked >= total // 2
 
