@@ -230,6 +230,17 @@ LSB_API int lsb_swiglu(const void* gu, void* out, int64_t S, int64_t I, int64_t 
                        int64_t ld_out, int dtype, void* stream);
 
 /*
+ * Greedy next token of every decode row: tokens[s] = argmax(logits[s, :V])
+ * (torch.argmax order: the first index of the maximum; NaN counts as the
+ * maximum), and positions[s] += 1 when positions is not NULL. logits is
+ * [S, V] with row stride ld (f32 / bf16 / fp16); tokens and positions are
+ * int64 [S]. Replaces `logits[:, -1].argmax(-1)` and the write of the next
+ * id in lightserve's decode loop (model/cuda_graph_decode.py:114-118).
+ */
+LSB_API int lsb_greedy_next(const void* logits, int64_t S, int64_t V, int64_t ld, int dtype,
+                            int64_t* tokens, int64_t* positions, void* stream);
+
+/*
  * Weight-streaming linear layer for decode batches: y[S, N] = x[S, K] @ W[K, N]
  * with fp32 accumulation and one rounding to dtype (bf16 or fp16).
  * Replaces the projections of lightserve's decode step, `h @ w` in

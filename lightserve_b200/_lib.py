@@ -64,6 +64,7 @@ SIGNATURES = {
     "lsb_rope_kv_write_slots": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
                                      _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "lsb_swiglu": (_I, [_P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lsb_greedy_next": (_I, [_P, _I64, _I64, _I64, _I, _P, _P, _P]),
     "lsb_linear_packed_bytes": (_I64, [_I64, _I64]),
     "lsb_linear_pack": (_I, [_P, _I64, _I64, _I64, _I, _P, _I64, _P]),
     "lsb_linear": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P]),

@@ -651,7 +651,8 @@ extern "C" int lsb_paged_decode_static_scratch(
 // each product and the sum rounded to the model dtype, as torch computes it)
 // followed by the cache write, the block-table slot lookup
 // (engine/block_manager.py:58-61) and the context-length update.
-// One CTA per sequence; threads walk (head, rotation pair).
+// Scalar form (any dtype, any alignment): one CTA per sequence, threads walk
+// (head, rotation pair); 16-bit aligned inputs take the vectorised form below.
 namespace lsb {
 
 template <typename T>
@@ -763,30 +764,23 @@ __global__ void rope_kv_write_slots_kernel(const T* __restrict__ qkv, int64_t s_
   }
 }
 
-// 16-byte vectorised form of rope_kv_write_slots_kernel for 16-bit types:
-// a thread rotates 8 consecutive pairs (i, i + D/2) of one head of one token
-// (16-byte loads of q, k, v, cos and sin, 16-byte stores); a 256-thread CTA
-// covers 256 / (H * D / 16) tokens. Same roundings as the scalar kernel.
+// 16-byte vectorised forms for 16-bit types: a thread rotates 8 consecutive
+// pairs (i, i + D/2) of one head of one token (16-byte loads of q, k, v, cos
+// and sin, 16-byte stores); a 256-thread CTA covers 256 / (H * D / 16)
+// tokens. Same roundings as the scalar kernels. The packed-prefill kernel
+// takes each token's cache slot from slot_mapping, the decode kernel derives
+// it from the sequence's block table and position (and sets its context
+// length).
 template <typename T>
-__global__ void __launch_bounds__(256)
-rope_kv_write_slots_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part, int64_t s_h,
-                               const T* __restrict__ cos_t, const T* __restrict__ sin_t,
-                               int64_t s_pos, const int64_t* __restrict__ positions,
-                               const int64_t* __restrict__ slot_mapping, T* __restrict__ q_out,
-                               T* __restrict__ k_out, T* __restrict__ k_cache,
-                               T* __restrict__ v_cache, int H, int D, int64_t T_tokens,
-                               int64_t num_slots, int bs) {
+__device__ __forceinline__ void rope_vec_lane(const T* __restrict__ qkv, int64_t s_s,
+                                              int64_t s_part, int64_t s_h,
+                                              const T* __restrict__ cos_t,
+                                              const T* __restrict__ sin_t, int64_t s_pos,
+                                              int64_t t, int h, int i0, int64_t pos, int64_t slot,
+                                              T* __restrict__ q_out, T* __restrict__ k_out,
+                                              T* __restrict__ k_cache, T* __restrict__ v_cache,
+                                              int H, int D, int bs) {
   const int half = D / 2;
-  const int lanes_per_token = H * half / 8;
-  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t t = g / lanes_per_token;
-  if (t >= T_tokens) return;
-  const int r = (int)(g - t * lanes_per_token);
-  const int h = r / (half / 8);
-  const int i0 = (r - h * (half / 8)) * 8;
-  const int64_t pos = positions[t];
-  const int64_t slot = slot_mapping[t];
-  const bool write = slot >= 0 && slot < num_slots;
   const Vec16<T> c0 = ld_vec16(cos_t + pos * s_pos + i0), c1 = ld_vec16(cos_t + pos * s_pos + i0 + half);
   const Vec16<T> n0 = ld_vec16(sin_t + pos * s_pos + i0), n1 = ld_vec16(sin_t + pos * s_pos + i0 + half);
   const T* qh = qkv + t * s_s + h * s_h;
@@ -815,13 +809,62 @@ rope_kv_write_slots_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s
     st_vec16(k_out + o, ok1);
     st_vec16(k_out + o + half, ok2);
   }
-  if (write) {
+  if (slot >= 0) {
     const int64_t dst = (((slot / bs) * H + h) * bs + slot % bs) * D + i0;
     st_vec16(k_cache + dst, ok1);
     st_vec16(k_cache + dst + half, ok2);
     st_vec16(v_cache + dst, ld_vec16(qh + 2 * s_part + i0));
     st_vec16(v_cache + dst + half, ld_vec16(qh + 2 * s_part + i0 + half));
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+rope_kv_write_slots_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                               const T* __restrict__ cos_t, const T* __restrict__ sin_t,
+                               int64_t s_pos, const int64_t* __restrict__ positions,
+                               const int64_t* __restrict__ slot_mapping, T* __restrict__ q_out,
+                               T* __restrict__ k_out, T* __restrict__ k_cache,
+                               T* __restrict__ v_cache, int H, int D, int64_t T_tokens,
+                               int64_t num_slots, int bs) {
+  const int half = D / 2;
+  const int lanes_per_token = H * half / 8;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t t = g / lanes_per_token;
+  if (t >= T_tokens) return;
+  const int r = (int)(g - t * lanes_per_token);
+  const int h = r / (half / 8);
+  const int i0 = (r - h * (half / 8)) * 8;
+  const int64_t slot = slot_mapping[t];
+  rope_vec_lane(qkv, s_s, s_part, s_h, cos_t, sin_t, s_pos, t, h, i0, positions[t],
+                (slot >= 0 && slot < num_slots) ? slot : -1, q_out, k_out, k_cache, v_cache, H, D,
+                bs);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+rope_kv_write_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part, int64_t s_h,
+                         const T* __restrict__ cos_t, const T* __restrict__ sin_t, int64_t s_pos,
+                         const int64_t* __restrict__ positions,
+                         const int32_t* __restrict__ block_tables, int max_blocks,
+                         T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache,
+                         int32_t* __restrict__ context_lens, int H, int D, int64_t S,
+                         int num_blocks, int bs) {
+  const int half = D / 2;
+  const int lanes_per_token = H * half / 8;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t s = g / lanes_per_token;
+  if (s >= S) return;
+  const int r = (int)(g - s * lanes_per_token);
+  const int h = r / (half / 8);
+  const int i0 = (r - h * (half / 8)) * 8;
+  const int64_t pos = positions[s];
+  const int64_t bidx = pos / bs;
+  const int blk = (bidx >= 0 && bidx < max_blocks) ? block_tables[s * max_blocks + bidx] : -1;
+  const int64_t slot = (blk >= 0 && blk < num_blocks) ? (int64_t)blk * bs + pos % bs : -1;
+  if (r == 0 && context_lens != nullptr) context_lens[s] = (int32_t)(pos + 1);
+  rope_vec_lane(qkv, s_s, s_part, s_h, cos_t, sin_t, s_pos, s, h, i0, pos, slot, q_out,
+                (T*)nullptr, k_cache, v_cache, H, D, bs);
 }
 
 }  // namespace lsb
@@ -886,6 +929,26 @@ extern "C" int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, i
                 "rope_kv_write: null pointer");
   LSB_CHECK_ARG(S <= 0x7fffffff, "rope_kv_write: S too large");
   cudaStream_t st = (cudaStream_t)stream;
+  const bool a16 = [&] {
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    return (D % 16) == 0 && al(qkv) && al(cos_table) && al(sin_table) && al(q_out) &&
+           al(k_cache) && al(v_cache) && (s_s * 2) % 16 == 0 && (s_part * 2) % 16 == 0 &&
+           (s_h * 2) % 16 == 0 && (s_pos * 2) % 16 == 0;
+  }();
+  if ((dtype == LSB_DTYPE_BF16 || dtype == LSB_DTYPE_F16) && a16) {
+    const int64_t lanes = S * H * D / 16;
+    const unsigned blocks = (unsigned)((lanes + 255) / 256);
+    auto launch = [&](auto tag) -> int {
+      using Tp = decltype(tag);
+      lsb::rope_kv_write_vec_kernel<Tp><<<blocks, 256, 0, st>>>(
+          (const Tp*)qkv, s_s, s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos,
+          positions, block_tables, (int)max_blocks_per_seq, (Tp*)q_out, (Tp*)k_cache,
+          (Tp*)v_cache, context_lens, (int)H, (int)D, S, (int)num_blocks, (int)block_size);
+      LSB_CHECK_LAUNCH("rope_kv_write");
+      return LSB_OK;
+    };
+    return dtype == LSB_DTYPE_BF16 ? launch(__nv_bfloat16()) : launch(__half());
+  }
   return LSB_DISPATCH_DTYPE(dtype, T, [&] {
     lsb::rope_kv_write_kernel<T><<<(unsigned)S, 256, 0, st>>>(
         (const T*)qkv, s_s, s_part, s_h, (const T*)cos_table, (const T*)sin_table, s_pos,

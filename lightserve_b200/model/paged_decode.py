@@ -45,6 +45,7 @@ from ..kernels.fused_swiglu import silu_and_mul
 from ..kernels.flash_attention import flash_attention_varlen
 from ..kernels.linear import MAX_ROWS as LINEAR_MAX_ROWS
 from ..kernels.linear import linear, pack_linear_weight
+from ..kernels.sampling import greedy_next
 from ..kernels.paged_attention import (paged_decode_attention, paged_decode_workspace,
                                         rope_kv_write, rope_kv_write_slots, write_kv_cache)
 from .minimal_llama import LlamaConfig, LlamaWeights, llama_forward, precompute_rope
@@ -310,9 +311,8 @@ class PagedDecoder:
             x = mm(silu_and_mul(gu, out=self.act), fz.w_down_t)
         final, _ = fused_add_rmsnorm(x, residual, self.w.norm_weight, eps=cfg.rms_eps)
         logits = mm(final, self.lm_head_t)
-        nxt = logits.argmax(-1)
-        self.tokens.copy_(nxt)
-        self.positions.add_(1)
+        # Next token of every row (argmax) into self.tokens, positions + 1.
+        greedy_next(logits, self.tokens, self.positions)
         return self.tokens
 
     def capture(self, warmup: int = 3):

@@ -97,21 +97,26 @@ def test_kv_write_exact_and_skips_negative_slots():
     assert int((kc != 0).any(-1).sum()) == (T - 1) * H
 
 
+@pytest.mark.parametrize("S,H,D", [(5, 4, 64), (64, 16, 128)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_fused_rope_kv_write_matches_eager_ops(dtype):
-    """lsb_rope_kv_write == lightserve-style apply_rope (torch ops) + cache write, bit for bit."""
+def test_fused_rope_kv_write_matches_eager_ops(dtype, S, H, D):
+    """lsb_rope_kv_write == lightserve-style apply_rope (torch ops) + cache write,
+    bit for bit (16-bit inputs take the vectorised kernel, fp32 the scalar one);
+    a row whose block table is empty (an idle decode row) writes no cache slot."""
     from lightserve_b200.kernels.paged_attention import rope_kv_write
     from lightserve_b200.model.minimal_llama import LlamaConfig, apply_rope, precompute_rope
 
     torch.manual_seed(0)
-    S, H, D, bs, mb = 5, 4, 64, 16, 6
+    bs, mb = 16, 6
     cfg = LlamaConfig(vocab_size=8, hidden_size=H * D, intermediate_size=8, n_layers=1, n_heads=H,
                       head_dim=D, max_seq_len=96, rope_theta=10000.0, dtype=dtype)
     cos, sin = precompute_rope(cfg, "cuda")
     qkv = torch.randn(S, 3, H, D, device="cuda").to(dtype)
-    pos = torch.tensor([0, 5, 17, 63, 95], device="cuda")
+    pos = torch.randint(0, 96, (S,), device="cuda")
+    pos[:5] = torch.tensor([0, 5, 17, 63, 95], device="cuda")
     nb = S * mb
     bt = torch.randperm(nb, device="cuda").view(S, mb).to(torch.int32)
+    bt[2] = -1  # idle row
     kc = torch.zeros(nb, H, bs, D, device="cuda", dtype=dtype); vc = torch.zeros_like(kc)
     q_out = torch.empty(S, H, D, device="cuda", dtype=dtype)
     cl = torch.zeros(S, dtype=torch.int32, device="cuda")
@@ -120,6 +125,7 @@ def test_fused_rope_kv_write_matches_eager_ops(dtype):
     q_ref, k_ref = apply_rope(qkv[:, 0], qkv[:, 1], cos[pos].unsqueeze(1), sin[pos].unsqueeze(1))
     kc2 = torch.zeros_like(kc); vc2 = torch.zeros_like(vc)
     slots = bt.gather(1, (pos // bs).unsqueeze(1)).squeeze(1).long() * bs + pos % bs
+    slots[2] = -1
     write_kv_cache(k_ref.contiguous(), qkv[:, 2], kc2, vc2, slots)
     assert torch.equal(q_out, q_ref)
     assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
