@@ -49,7 +49,8 @@ struct Strides4 {
 };
 template <typename T>
 int launch_dsum(const void* o, const void* dout, float* dsum, int64_t B, int64_t H, int64_t N,
-                int64_t D, Strides4 so, Strides4 sdo, cudaStream_t st);
+                int64_t D, Strides4 so, Strides4 sdo, cudaStream_t st, float* zero_rows,
+                int* zero_counter, bool* zeroed);
 template <typename T>
 int launch_dq_cast(const float* dq_acc, void* dq, int64_t B, int64_t H, int64_t N, int64_t D,
                    Strides4 sdq, cudaStream_t st);
@@ -720,14 +721,19 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
                 float* dq_acc, cudaStream_t st) {
   auto S4 = [](const int64_t* s) { return Strides4{s[0], s[1], s[2], s[3]}; };
   const bool bf = dtype == LSB_DTYPE_BF16;
-  int rc = bf ? launch_dsum<__nv_bfloat16>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st)
-              : launch_dsum<__half>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st);
-  if (rc) return rc;
   // The work-item counter sits in the 256 bytes after the (256-byte padded)
-  // dQ accumulator (lsb_attn_bwd_workspace_size); one memset zeroes both.
+  // dQ accumulator (lsb_attn_bwd_workspace_size). The Dsum pass zeroes both
+  // in the same launch (else one memset does).
   int* work_counter = reinterpret_cast<int*>(reinterpret_cast<char*>(dq_acc) + align256(4 * B * H * N * D));
-  LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, (size_t)align256(4 * B * H * N * D) + sizeof(int), st),
-              "attn_bwd dQ accumulator memset");
+  bool zeroed = false;
+  int rc = bf ? launch_dsum<__nv_bfloat16>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st, dq_acc,
+                                           work_counter, &zeroed)
+              : launch_dsum<__half>(o, dout, dsum, B, H, N, D, S4(so), S4(sdo), st, dq_acc,
+                                    work_counter, &zeroed);
+  if (rc) return rc;
+  if (!zeroed)
+    LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, (size_t)align256(4 * B * H * N * D) + sizeof(int), st),
+                "attn_bwd dQ accumulator memset");
   rc = bf ? launch_fa_bwd<1>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,
                              causal, dtype, dsum, dq_acc, work_counter, st)
           : launch_fa_bwd<0>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,

@@ -334,7 +334,8 @@ __global__ void attn_dsum_rows_kernel(const T* __restrict__ o, const T* __restri
 template <typename T, int LPR>
 __global__ void __launch_bounds__(256)
 attn_dsum_vec_kernel(const T* __restrict__ o, const T* __restrict__ dout, float* __restrict__ dsum,
-                     int H, int N, Strides4 so, Strides4 sdo, int64_t rows) {
+                     int H, int N, Strides4 so, Strides4 sdo, int64_t rows,
+                     float* __restrict__ zero_rows, int* __restrict__ zero_counter) {
   constexpr int VEC = 16 / sizeof(T);
   const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LPR;
   const int sub = threadIdx.x % LPR;
@@ -347,7 +348,14 @@ attn_dsum_vec_kernel(const T* __restrict__ o, const T* __restrict__ dout, float*
     Vec16<T> c = ld_vec16_stream(dout + b * sdo.b + h * sdo.h + m * sdo.n + sub * VEC);
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc = fmaf(to_f(a.v[j]), to_f(c.v[j]), acc);
+    if (zero_rows != nullptr) {
+      // The same row of the dense fp32 dQ accumulator ([rows][LPR * VEC]).
+      float4* z = reinterpret_cast<float4*>(zero_rows + row * (LPR * VEC)) + sub * (VEC / 4);
+#pragma unroll
+      for (int j = 0; j < VEC / 4; ++j) z[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
+  if (zero_counter != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero_counter = 0;
 #pragma unroll
   for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (ok && sub == 0) dsum[row] = acc;
@@ -367,12 +375,18 @@ __global__ void attn_dq_cast_vec_kernel(const float4* __restrict__ src, uint4* _
   }
 }
 
+// Dsum pass. When zero_rows is given (the dense fp32 dQ accumulator) and
+// the vectorised kernel applies, the same launch zeroes it and *zero_counter
+// (the backward kernel's work counter) and sets *zeroed; the caller zeroes
+// them itself otherwise.
 template <typename T>
 int launch_dsum(const void* o, const void* dout, float* dsum, int64_t B, int64_t H, int64_t N,
-                int64_t D, Strides4 so, Strides4 sdo, cudaStream_t st) {
+                int64_t D, Strides4 so, Strides4 sdo, cudaStream_t st, float* zero_rows,
+                int* zero_counter, bool* zeroed) {
   const int64_t rows = B * H * N;
   const int threads = 256;
   constexpr int VEC = 16 / sizeof(T);
+  if (zeroed) *zeroed = false;
   const bool vec = so.d == 1 && sdo.d == 1 && aligned16(o) && aligned16(dout) &&
                    (so.n * sizeof(T)) % 16 == 0 && (so.h * sizeof(T)) % 16 == 0 &&
                    (so.b * sizeof(T)) % 16 == 0 && (sdo.n * sizeof(T)) % 16 == 0 &&
@@ -380,13 +394,16 @@ int launch_dsum(const void* o, const void* dout, float* dsum, int64_t B, int64_t
   if (vec && (D == 16 * VEC || D == 8 * VEC)) {
     const int lpr = (int)(D / VEC);
     const int64_t blocks = (rows * lpr + threads - 1) / threads;
+    float* z = (zero_rows != nullptr && aligned16(zero_rows)) ? zero_rows : nullptr;
+    int* zc = z != nullptr ? zero_counter : nullptr;
     if (lpr == 16)
       attn_dsum_vec_kernel<T, 16><<<(unsigned)blocks, threads, 0, st>>>(
-          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows);
+          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows, z, zc);
     else
       attn_dsum_vec_kernel<T, 8><<<(unsigned)blocks, threads, 0, st>>>(
-          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows);
+          (const T*)o, (const T*)dout, dsum, (int)H, (int)N, so, sdo, rows, z, zc);
     LSB_CHECK_LAUNCH("attn_bwd_dsum");
+    if (zeroed) *zeroed = z != nullptr;
     return LSB_OK;
   }
   const int64_t blocks = (rows * 32 + threads - 1) / threads;
@@ -428,10 +445,12 @@ static int launch_bwd_simt(const void* q, const void* k, const void* v, const vo
                            Strides4 sv, Strides4 so, Strides4 sdo, Strides4 sdq, Strides4 sdk,
                            Strides4 sdv, float scale, int causal, float* dsum, float* dq_acc,
                            cudaStream_t st) {
-  int rc = launch_dsum<T>(o, dout, dsum, B, H, N, D, so, sdo, st);
+  bool zeroed = false;
+  int rc = launch_dsum<T>(o, dout, dsum, B, H, N, D, so, sdo, st, dq_acc, nullptr, &zeroed);
   if (rc) return rc;
-  LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)(B * H * N * D), st),
-              "attn_bwd dQ accumulator memset");
+  if (!zeroed)
+    LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)(B * H * N * D), st),
+                "attn_bwd dQ accumulator memset");
   const int Dp = (int)((D + 7) / 8 * 8);
   const size_t smem =
       sizeof(float) * (size_t)(2 * BS_BN * Dp + 2 * BS_BM * Dp + 2 * BS_BM * BS_BN + 2 * BS_BM);
@@ -447,9 +466,10 @@ static int launch_bwd_simt(const void* q, const void* k, const void* v, const vo
 
 // Explicit instantiations used by the tcgen05 backward path (attn_bwd_sm100.cu).
 template int launch_dsum<__nv_bfloat16>(const void*, const void*, float*, int64_t, int64_t,
-                                        int64_t, int64_t, Strides4, Strides4, cudaStream_t);
+                                        int64_t, int64_t, Strides4, Strides4, cudaStream_t,
+                                        float*, int*, bool*);
 template int launch_dsum<__half>(const void*, const void*, float*, int64_t, int64_t, int64_t,
-                                 int64_t, Strides4, Strides4, cudaStream_t);
+                                 int64_t, Strides4, Strides4, cudaStream_t, float*, int*, bool*);
 template int launch_dq_cast<__nv_bfloat16>(const float*, void*, int64_t, int64_t, int64_t,
                                            int64_t, Strides4, cudaStream_t);
 template int launch_dq_cast<__half>(const float*, void*, int64_t, int64_t, int64_t, int64_t,
