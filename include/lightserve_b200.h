@@ -67,6 +67,15 @@ LSB_API int lsb_device_error_reset(void);
  * reference. */
 LSB_API int lsb_selftest_bounded_wait(int* status, void* stream);
 
+/* Process-wide switch for programmatic dependent launch (default on): the
+ * norm, SwiGLU, RoPE/KV-write, paged-decode, greedy-sampling and linear
+ * kernels are launched so that each may start while the previous kernel of
+ * its stream finishes, and each waits (griddepcontrol.wait) for that kernel's
+ * completion before it touches memory -- this hides launch gaps inside a
+ * decode step. Results do not depend on it. Returns the previous setting.
+ * No counterpart in the reference. */
+LSB_API int lsb_set_programmatic_launch(int enable);
+
 /* Library version string. */
 LSB_API const char* lsb_version(void);
 

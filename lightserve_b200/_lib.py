@@ -44,6 +44,7 @@ SIGNATURES = {
     "lsb_version": (ctypes.c_char_p, []),
     "lsb_device_error": (_I, []),
     "lsb_device_error_reset": (_I, []),
+    "lsb_set_programmatic_launch": (_I, [_I]),
     "lsb_selftest_bounded_wait": (_I, [_P, _P]),
     "lsb_rmsnorm_residual": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
     "lsb_attn_fwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64P, _I64P, _I64P, _I64P,

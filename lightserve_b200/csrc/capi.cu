@@ -63,6 +63,15 @@ int linear_device_error(bool reset);
 
 extern "C" const char* lsb_last_error(void) { return lsb::g_err; }
 
+namespace lsb {
+static std::atomic<int> g_programmatic_launch{1};
+bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
+}  // namespace lsb
+
+extern "C" int lsb_set_programmatic_launch(int enable) {
+  return lsb::g_programmatic_launch.exchange(enable ? 1 : 0);
+}
+
 static int device_error_all(bool reset) {
   int e = 0;
   for (int v : {lsb::attn_fwd_tc_device_error(reset), lsb::attn_bwd_tc_device_error(reset),

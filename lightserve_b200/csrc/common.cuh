@@ -16,6 +16,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <utility>
 
 #include "../../include/lightserve_b200.h"
 
@@ -205,6 +206,36 @@ __device__ __forceinline__ float warp_max(float v) {
 // this kernel's completion before reading its results). No effect otherwise.
 __device__ __forceinline__ void allow_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Waits until the kernels this one depends on (the previous kernel of the
+// stream, when this one was launched with programmatic stream serialisation)
+// have completed and their writes are visible. Returns at once otherwise.
+// Every kernel launched through launch_kernel() executes it before it reads
+// its inputs or writes its outputs.
+__device__ __forceinline__ void wait_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Process-wide switch (lsb_set_programmatic_launch, default on): kernels
+// launched through launch_kernel() may start while the previous kernel of
+// the stream finishes, hiding the launch gap between consecutive kernels.
+bool programmatic_launch();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic_launch() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -169,6 +169,7 @@ linear_wstream_kernel(const __grid_constant__ CUtensorMap tx, const Params p) {
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(send_ok + 1);
   float* recv = reinterpret_cast<float*>(smem + p.recv_off);  // [split][rows of this rank][SP]
 
+  allow_dependents();  // the next kernel may launch; it waits for this one's completion
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = p.split;
   const int rank = (int)cluster_rank();

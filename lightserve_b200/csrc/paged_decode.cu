@@ -190,6 +190,7 @@ paged_decode_combine_kernel(const int32_t* __restrict__ context_lens, int max_to
                             const float* __restrict__ part_m, const float* __restrict__ part_l,
                             const float* __restrict__ part_acc) {
   allow_dependents();
+  wait_prerequisites();
   const int h = blockIdx.x, s = blockIdx.y;
   const int ctx = max(0, min(context_lens[s], max_tokens));
   const int nparts = (ctx + PD_PART_TOKENS - 1) / PD_PART_TOKENS;
@@ -228,6 +229,7 @@ paged_decode_bulk_kernel(const T* __restrict__ q, const T* __restrict__ k_cache,
                          int64_t so_h, float scale_log2, int max_parts, float* __restrict__ part_m,
                          float* __restrict__ part_l, float* __restrict__ part_acc) {
   allow_dependents();
+  wait_prerequisites();
   using namespace sm100;
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LPT = D / VEC;                    // lanes per token row
@@ -415,9 +417,11 @@ static int launch_paged_decode(const void* q, const void* kc, const void* vc,
   bool launched = false;
   if constexpr (PD_BS * D * sizeof(T) * 2 * PD_STAGES <= 40 * 1024) {
     if (bs_log2 == 4 && aligned16(kc) && aligned16(vc)) {
-      paged_decode_bulk_kernel<T, D><<<grid, (PD_WARPS + 1) * 32, 0, st>>>(
-          (const T*)q, (const T*)kc, (const T*)vc, bt, cl, (T*)o, (int)H, (int)max_blocks,
-          (int)num_blocks, sq_s, sq_h, so_s, so_h, scale * PD_LOG2E, (int)P, pm, pl, pa);
+      LSB_CUDA_OK(launch_kernel(paged_decode_bulk_kernel<T, D>, grid, dim3((PD_WARPS + 1) * 32), 0,
+                                st, (const T*)q, (const T*)kc, (const T*)vc, bt, cl, (T*)o, (int)H,
+                                (int)max_blocks, (int)num_blocks, sq_s, sq_h, so_s, so_h,
+                                scale * PD_LOG2E, (int)P, pm, pl, pa),
+                  "paged_decode");
       launched = true;
     }
   }
@@ -427,9 +431,11 @@ static int launch_paged_decode(const void* q, const void* kc, const void* vc,
       sq_s, sq_h, so_s, so_h, scale * PD_LOG2E, (int)P, pm, pl, pa);
   LSB_CHECK_LAUNCH("paged_decode");
   if (P > 1) {
-    paged_decode_combine_kernel<T, D><<<dim3((unsigned)H, (unsigned)S), 128, 0, st>>>(
-        cl, (int)(max_blocks << bs_log2), (T*)o, (int)H, so_s, so_h, (int)P, pm, pl, pa);
-    LSB_CHECK_LAUNCH("paged_decode_combine");
+    LSB_CUDA_OK(launch_kernel(paged_decode_combine_kernel<T, D>, dim3((unsigned)H, (unsigned)S),
+                              dim3(128), 0, st, (const int32_t*)cl, (int)(max_blocks << bs_log2),
+                              (T*)o, (int)H, so_s, so_h, (int)P, (const float*)pm,
+                              (const float*)pl, (const float*)pa),
+                "paged_decode_combine");
   }
   return LSB_OK;
 }
@@ -850,6 +856,8 @@ rope_kv_write_vec_kernel(const T* __restrict__ qkv, int64_t s_s, int64_t s_part,
                          T* __restrict__ q_out, T* __restrict__ k_cache, T* __restrict__ v_cache,
                          int32_t* __restrict__ context_lens, int H, int D, int64_t S,
                          int num_blocks, int bs) {
+  allow_dependents();
+  wait_prerequisites();
   const int half = D / 2;
   const int lanes_per_token = H * half / 8;
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -940,11 +948,11 @@ extern "C" int lsb_rope_kv_write(const void* qkv, int64_t s_s, int64_t s_part, i
     const unsigned blocks = (unsigned)((lanes + 255) / 256);
     auto launch = [&](auto tag) -> int {
       using Tp = decltype(tag);
-      lsb::rope_kv_write_vec_kernel<Tp><<<blocks, 256, 0, st>>>(
-          (const Tp*)qkv, s_s, s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos,
-          positions, block_tables, (int)max_blocks_per_seq, (Tp*)q_out, (Tp*)k_cache,
-          (Tp*)v_cache, context_lens, (int)H, (int)D, S, (int)num_blocks, (int)block_size);
-      LSB_CHECK_LAUNCH("rope_kv_write");
+      LSB_CUDA_OK(lsb::launch_kernel(
+          lsb::rope_kv_write_vec_kernel<Tp>, dim3(blocks), dim3(256), 0, st, (const Tp*)qkv, s_s,
+          s_part, s_h, (const Tp*)cos_table, (const Tp*)sin_table, s_pos, positions,
+          block_tables, (int)max_blocks_per_seq, (Tp*)q_out, (Tp*)k_cache, (Tp*)v_cache,
+          context_lens, (int)H, (int)D, S, (int)num_blocks, (int)block_size), "rope_kv_write");
       return LSB_OK;
     };
     return dtype == LSB_DTYPE_BF16 ? launch(__nv_bfloat16()) : launch(__half());

@@ -23,6 +23,7 @@ rmsnorm_residual_vec_kernel(const T* __restrict__ x, const T* __restrict__ r,
                             T* __restrict__ h_out, int N, int64_t ld_x,
                             int64_t ld_r, int64_t ld_o, int64_t ld_h, float eps) {
   allow_dependents();
+  wait_prerequisites();
   constexpr int VEC = Vec16<T>::N;
   const int row = blockIdx.x;
   const int nvec = N / VEC;
@@ -137,13 +138,13 @@ static int launch_rmsnorm(const void* x, const void* r, const void* w, void* out
     T* op = (T*)out; T* hp = (T*)h;
     dim3 grid((unsigned)M);
     if (need <= 1)
-      rmsnorm_residual_vec_kernel<T, 1><<<grid, threads, 0, st>>>(xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps);
+      LSB_CUDA_OK(launch_kernel(rmsnorm_residual_vec_kernel<T, 1>, grid, dim3(threads), 0, st, xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps), "rmsnorm_residual");
     else if (need <= 2)
-      rmsnorm_residual_vec_kernel<T, 2><<<grid, threads, 0, st>>>(xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps);
+      LSB_CUDA_OK(launch_kernel(rmsnorm_residual_vec_kernel<T, 2>, grid, dim3(threads), 0, st, xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps), "rmsnorm_residual");
     else if (need <= 4)
-      rmsnorm_residual_vec_kernel<T, 4><<<grid, threads, 0, st>>>(xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps);
+      LSB_CUDA_OK(launch_kernel(rmsnorm_residual_vec_kernel<T, 4>, grid, dim3(threads), 0, st, xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps), "rmsnorm_residual");
     else
-      rmsnorm_residual_vec_kernel<T, 8><<<grid, threads, 0, st>>>(xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps);
+      LSB_CUDA_OK(launch_kernel(rmsnorm_residual_vec_kernel<T, 8>, grid, dim3(threads), 0, st, xp, rp, wp, op, hp, (int)N, ld_x, ld_r, ld_o, ld_h, eps), "rmsnorm_residual");
   } else {
     rmsnorm_residual_scalar_kernel<T><<<(unsigned)M, 256, 0, st>>>(
         (const T*)x, (const T*)r, (const T*)w, (T*)out, (T*)h, N, ld_x, ld_r, ld_o, ld_h, eps);

@@ -24,6 +24,7 @@ __global__ void __launch_bounds__(256)
 greedy_next_kernel(const T* __restrict__ logits, int64_t ld, int V, int64_t* __restrict__ tokens,
                    int64_t* __restrict__ positions) {
   allow_dependents();
+  wait_prerequisites();
   const T* row = logits + (int64_t)blockIdx.x * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -72,9 +73,9 @@ extern "C" int lsb_greedy_next(const void* logits, int64_t S, int64_t V, int64_t
   LSB_CHECK_ARG(S <= 0x7fffffff && V <= 0x7fffffff, "greedy_next: shape too large");
   cudaStream_t st = (cudaStream_t)stream;
   return LSB_DISPATCH_DTYPE(dtype, T, [&] {
-    lsb::greedy_next_kernel<T><<<(unsigned)S, 256, 0, st>>>((const T*)logits, ld, (int)V, tokens,
-                                                          positions);
-    LSB_CHECK_LAUNCH("greedy_next");
+    LSB_CUDA_OK(lsb::launch_kernel(lsb::greedy_next_kernel<T>, dim3((unsigned)S), dim3(256), 0, st,
+                                   (const T*)logits, ld, (int)V, tokens, positions),
+                "greedy_next");
     return LSB_OK;
   });
 }

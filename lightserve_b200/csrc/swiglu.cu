@@ -26,6 +26,7 @@ template <typename T>
 __global__ void swiglu_vec_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t S,
                                   int64_t I, int64_t ld_gu, int64_t ld_out) {
   allow_dependents();
+  wait_prerequisites();
   constexpr int VEC = Vec16<T>::N;
   const int64_t nv = I / VEC;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < S * nv;
@@ -60,8 +61,9 @@ static int launch_swiglu(const void* gu, void* out, int64_t S, int64_t I, int64_
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((work + threads - 1) / threads, (int64_t)num_sms() * 8);
   if (vec)
-    swiglu_vec_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(
-        static_cast<const T*>(gu), static_cast<T*>(out), S, I, ld_gu, ld_out);
+    LSB_CUDA_OK(launch_kernel(swiglu_vec_kernel<T>, dim3((unsigned)blocks), dim3(threads), 0, st,
+                              static_cast<const T*>(gu), static_cast<T*>(out), S, I, ld_gu, ld_out),
+                "swiglu");
   else
     swiglu_scalar_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(
         static_cast<const T*>(gu), static_cast<T*>(out), S, I, ld_gu, ld_out);
