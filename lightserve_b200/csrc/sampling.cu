@@ -4,8 +4,8 @@
 // write of the next id (model/cuda_graph_decode.py:114-118; torch.argmax:
 // the first index of the maximum, a NaN counts as the maximum) and, for the
 // paged decode runner, the position increment of every sequence -- one
-// launch instead of three torch kernels. One CTA per row; 16-byte loads when
-// the row is aligned.
+// launch instead of three torch kernels. One 1024-thread CTA per row; 16-byte
+// loads when the row is aligned.
 #include "common.cuh"
 
 namespace lsb {
@@ -20,7 +20,7 @@ __device__ __forceinline__ bool argmax_better(float a, int ia, float b, int ib) 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
 greedy_next_kernel(const T* __restrict__ logits, int64_t ld, int V, int64_t* __restrict__ tokens,
                    int64_t* __restrict__ positions) {
   allow_dependents();
@@ -31,12 +31,26 @@ greedy_next_kernel(const T* __restrict__ logits, int64_t ld, int V, int64_t* __r
   constexpr int VEC = 16 / sizeof(T);
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const int nv = vec ? V / VEC : 0;
-  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
-    const Vec16<T> v = ld_vec16_stream(row + c * VEC);
+  // Four 16-byte loads in flight per thread before any is consumed: one
+  // row is only ~64 KiB, so the time is load latency, not bandwidth.
+  constexpr int U = 4;
+  for (int c0 = threadIdx.x; c0 < nv; c0 += U * blockDim.x) {
+    Vec16<T> v[U];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const float f = to_f(v.v[j]);
-      if (argmax_better(f, c * VEC + j, best, bi)) { best = f; bi = c * VEC + j; }
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * blockDim.x;
+      if (c < nv) v[u] = ld_vec16_stream(row + c * VEC);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * blockDim.x;
+      if (c < nv) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float f = to_f(v[u].v[j]);
+          if (argmax_better(f, c * VEC + j, best, bi)) { best = f; bi = c * VEC + j; }
+        }
+      }
     }
   }
   for (int i = nv * VEC + threadIdx.x; i < V; i += blockDim.x) {
@@ -49,8 +63,8 @@ greedy_next_kernel(const T* __restrict__ logits, int64_t ld, int V, int64_t* __r
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
     if (argmax_better(ob, oi, best, bi)) { best = ob; bi = oi; }
   }
-  __shared__ float sb[8];
-  __shared__ int si[8];
+  __shared__ float sb[32];
+  __shared__ int si[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) { sb[warp] = best; si[warp] = bi; }
   __syncthreads();
@@ -73,7 +87,7 @@ extern "C" int lsb_greedy_next(const void* logits, int64_t S, int64_t V, int64_t
   LSB_CHECK_ARG(S <= 0x7fffffff && V <= 0x7fffffff, "greedy_next: shape too large");
   cudaStream_t st = (cudaStream_t)stream;
   return LSB_DISPATCH_DTYPE(dtype, T, [&] {
-    LSB_CUDA_OK(lsb::launch_kernel(lsb::greedy_next_kernel<T>, dim3((unsigned)S), dim3(256), 0, st,
+    LSB_CUDA_OK(lsb::launch_kernel(lsb::greedy_next_kernel<T>, dim3((unsigned)S), dim3(1024), 0, st,
                                    (const T*)logits, ld, (int)V, tokens, positions),
                 "greedy_next");
     return LSB_OK;

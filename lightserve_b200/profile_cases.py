@@ -10,6 +10,8 @@ launch of exactly that kernel. Cases:
 * ``varlen``  causal flash_attention_varlen over ``--lens`` packed sequences
 * ``rmsnorm`` fused_add_rmsnorm on [M, N] bf16
 * ``decode``  paged_decode_attention, S sequences with contexts U[lo, hi]
+* ``linear``  lsb_linear, x [S, K] @ W [K, N] bf16 (weight packed once)
+* ``greedy``  greedy_next over [S, N] bf16 logits
 """
 from __future__ import annotations
 
@@ -20,7 +22,7 @@ import torch
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["fwd", "bwd", "varlen", "rmsnorm", "decode"])
+    ap.add_argument("case", choices=["fwd", "bwd", "varlen", "rmsnorm", "decode", "linear", "greedy"])
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--B", type=int, default=2)
     ap.add_argument("--H", type=int, default=32)
@@ -55,6 +57,17 @@ def main(argv=None):
         q, k, v = (rn(T, a.H, a.D) for _ in range(3))
         cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
         run = lambda: flash_attention_varlen(q, k, v, cu, max(lens), causal=True)  # noqa: E731
+    elif a.case == "linear":
+        from lightserve_b200.kernels import linear, pack_linear_weight
+        x = rn(a.S, a.D)  # K = --D
+        pw = pack_linear_weight((0.02 * rn(a.N, a.D)).contiguous())
+        out = torch.empty(a.S, a.N, device="cuda", dtype=bf)
+        run = lambda: linear(x, pw, out=out)  # noqa: E731
+    elif a.case == "greedy":
+        from lightserve_b200.kernels import greedy_next
+        logits = rn(a.S, a.N)
+        tok = torch.empty(a.S, dtype=torch.int64, device="cuda")
+        run = lambda: greedy_next(logits, tok)  # noqa: E731
     elif a.case == "rmsnorm":
         x, r = rn(a.M, a.N), rn(a.M, a.N)
         w = (1 + 0.02 * torch.randn(a.N, device="cuda", generator=g)).to(bf)
