@@ -61,39 +61,42 @@ using namespace sm100;
 
 constexpr int BN = 128;   // keys per CTA (TMEM lanes)
 constexpr int BM = 128;   // query rows per inner tile
-constexpr int D = 128;    // head dim served by this kernel
 constexpr int THREADS = 384;
 constexpr int CHUNK = 128 * 128;  // [128 rows][64 cols] 16-bit box, 128-byte swizzle
-constexpr int KC = D / 64;        // chunks per K, V, Q or dO tile
-constexpr int TILE = KC * CHUNK;  // 32 KiB
-
-constexpr int K_OFF = 0;
-constexpr int V_OFF = K_OFF + TILE;
-constexpr int NQS = 2;    // Q / statistics ring stages
-constexpr int Q_OFF = V_OFF + TILE;             // [NQS] Q tiles
-constexpr int DO_OFF = Q_OFF + NQS * TILE;      // dO tile
-constexpr int DS_OFF = DO_OFF + TILE;           // dS^T [2 chunks][128 keys][64 q]; dQ staging 1
-constexpr int STG_OFF = DS_OFF + TILE;          // dQ staging 0
-constexpr int STAGE_ROWS = 64;                  // dQ rows per staging buffer (64 x D fp32 = 32 KiB)
-static_assert(STAGE_ROWS * D * 4 == TILE, "a dQ staging buffer holds half a query tile");
-constexpr int STAT_OFF = STG_OFF + TILE;        // [NQS][2][BM] floats: lse2, dsum
-constexpr int BAR_OFF = STAT_OFF + NQS * 2 * BM * 4;
+constexpr int NQS = 2;            // Q / statistics ring stages
+constexpr int STAGE_ROWS = 64;    // dQ rows per staging buffer
+constexpr int NIS = 4;            // work-item id ring slots
 // k_full, v_full, k_empty, q_full[NQS], q_empty[NQS], stat_full[NQS], do_full, do_empty,
 // s_ready, p_ready, dp_ready, ds_ready, dq_ready, dq_free, dk_done, red_full[2],
 // red_free[2], epi_staged, epi_v_free, vdo_issued, epi_q_free[NQS], item_full[NIS],
 // item_empty[NIS]
-constexpr int NIS = 4;    // work-item id ring slots
 constexpr int NBAR = 3 + 4 * NQS + 16 + 2 * NIS;
-constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
-constexpr int ITEM_OFF = SLOT_OFF + 16;         // [NIS] work-item ids
-constexpr int SMEM = ITEM_OFF + NIS * 4;
-static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KiB shared-memory limit");
+
+// Shared-memory plan for head dim D (64 or 128): K, V, NQS Q tiles and dO
+// (D / 64 chunks each), the dS^T tile (two 64-query chunks, also dQ staging
+// 1), dQ staging 0 (64 rows x D fp32), the per-stage statistics, barriers.
+template <int D_>
+struct Layout {
+  static constexpr int D = D_;
+  static constexpr int KC = D / 64;        // chunks per K, V, Q or dO tile
+  static constexpr int TILE = KC * CHUNK;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + TILE;  // directly after K (see the dQ^T MMA)
+  static constexpr int Q_OFF = V_OFF + TILE;
+  static constexpr int DO_OFF = Q_OFF + NQS * TILE;
+  static constexpr int DS_OFF = DO_OFF + TILE;
+  static constexpr int STG_OFF = DS_OFF + 2 * CHUNK;
+  static constexpr int STAT_OFF = STG_OFF + STAGE_ROWS * D * 4;
+  static constexpr int BAR_OFF = STAT_OFF + NQS * 2 * BM * 4;
+  static constexpr int SLOT_OFF = BAR_OFF + NBAR * 8;
+  static constexpr int ITEM_OFF = SLOT_OFF + 16;  // [NIS] work-item ids
+  static constexpr int SMEM = ITEM_OFF + NIS * 4;
+  static_assert(STAGE_ROWS * D * 4 <= 2 * CHUNK, "dQ staging 1 lives in the dS^T tile");
+  static_assert(SMEM <= 232448, "backward tile set exceeds the 227 KiB shared-memory limit");
+};
 
 constexpr uint32_t T_DV = 0, T_DK = 128, T_S = 256, T_DP = 384;
-#ifndef LSB_BWD_GROUP
-#define LSB_BWD_GROUP 16
-#endif
-constexpr int BH_GROUP = LSB_BWD_GROUP;  // (batch, head) slices scheduled together
+constexpr int BH_GROUP = 16;  // (batch, head) slices scheduled together
 
 struct Params {
   const float* lse;
@@ -146,7 +149,7 @@ __device__ __forceinline__ Item decode_item(int item, const Params& p) {
 // per-tile barrier completes once per query tile, so its phase is the
 // CTA-wide running tile count g (across items), and k_full / v_full /
 // k_empty / epi_staged / epi_v_free complete once per item.
-template <int FMT>
+template <int FMT, int HD>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
               const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
@@ -155,6 +158,11 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   // No static shared memory is declared, so the dynamic block starts at the
   // (1 KiB-aligned) base of the CTA's window; the 128-byte swizzle needs
   // 1 KiB-aligned tiles and there is no room left for realignment padding.
+  using L = Layout<HD>;
+  constexpr int D = HD, KC = L::KC, TILE = L::TILE;
+  constexpr int K_OFF = L::K_OFF, V_OFF = L::V_OFF, Q_OFF = L::Q_OFF, DO_OFF = L::DO_OFF;
+  constexpr int DS_OFF = L::DS_OFF, STG_OFF = L::STG_OFF, STAT_OFF = L::STAT_OFF;
+  constexpr int BAR_OFF = L::BAR_OFF, SLOT_OFF = L::SLOT_OFF, ITEM_OFF = L::ITEM_OFF;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0) atomicCAS(&g_lsb_device_error, 0, 0xB00);
@@ -363,7 +371,10 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, BM, FMT, 0, 0);   // K-major A and B
       constexpr uint32_t ID_ACC = idesc_f16(128, D, FMT, 0, 1);  // TS; B (dO, Q) MN-major
-      constexpr uint32_t ID_DQ = idesc_f16(128, BM, FMT, 1, 1);  // A (K^T), B (dS^T) MN-major
+      // A (K^T), B (dS^T) MN-major. M stays 128 when D = 64: A's second
+      // 64-row group is then read from the V tile after K, and the TMEM
+      // lanes 64-127 it produces are never read.
+      constexpr uint32_t ID_DQ = idesc_f16(128, BM, FMT, 1, 1);
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO), ds_base = smem_u32(sDS);
       // X^T = A B^T with A the [128][D] K or V tile, B the [BM][D] Q or dO tile.
@@ -611,7 +622,8 @@ fa_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         }
         float* stage = reinterpret_cast<float*>(half == 0 ? sSTG : sDS);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) stage[c * D + r] = __uint_as_float(sv[c]) * p.scale;
+        for (int c = 0; c < 64; ++c)
+          if (D == 128 || r < D) stage[c * D + r] = __uint_as_float(sv[c]) * p.scale;
         fence_proxy_async_smem();
         mbar_arrive(&red_full[half]);
       }
@@ -670,7 +682,7 @@ bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const voi
                           const int64_t* sdv, int dtype) {
   (void)o; (void)so; (void)dq; (void)sdq;
   if (dtype != LSB_DTYPE_BF16 && dtype != LSB_DTYPE_F16) return false;
-  if (D != fa_bwd::D) return false;
+  if (D != 64 && D != 128) return false;
   if (N >= (1LL << 30) || B * H * ((N + fa_bwd::BN - 1) / fa_bwd::BN) > 0x7fffffff) return false;
   if (!tma_ok(q, B, H, N, sq, 2) || !tma_ok(k, B, H, N, sk, 2) || !tma_ok(v, B, H, N, sv, 2) ||
       !tma_ok(dout, B, H, N, sdo, 2))
@@ -679,7 +691,7 @@ bool attn_bwd_tc_eligible(const void* q, const void* k, const void* v, const voi
   return tma_ok(dk, B, H, N, sdk, 2) && tma_ok(dv, B, H, N, sdv, 2);
 }
 
-template <int FMT>
+template <int FMT, int HD>
 static int launch_fa_bwd(const void* q, const void* k, const void* v, const void* dout,
                          const float* lse, void* dk, void* dv, int64_t B, int64_t H, int64_t N,
                          const int64_t* sq, const int64_t* sk, const int64_t* sv,
@@ -687,6 +699,8 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
                          int causal, int dtype, const float* dsum, float* dq_acc,
                          int* work_counter, cudaStream_t st) {
   using namespace fa_bwd;
+  constexpr int D = HD;
+  constexpr int SMEM = Layout<HD>::SMEM;
   CUtensorMap mq, mk, mv, mdo, mdk, mdv;
   int rc = make_bhnd_map(&mq, q, dtype, B, H, N, D, sq, 64, BM);
   if (!rc) rc = make_bhnd_map(&mdo, dout, dtype, B, H, N, D, sdo, 64, BM);
@@ -702,7 +716,7 @@ static int launch_fa_bwd(const void* q, const void* k, const void* v, const void
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
-  auto kern = fa_bwd_kernel<FMT>;
+  auto kern = fa_bwd_kernel<FMT, HD>;
   static SmemLimit smem_limit;
   if (int rc_ = smem_limit.ensure(kern, SMEM, "attn_bwd_tc smem attribute")) return rc_;
   // Persistent: one CTA per SM (shared memory and TMEM allow no more).
@@ -734,10 +748,10 @@ int attn_bwd_tc(const void* q, const void* k, const void* v, const void* o, cons
   if (!zeroed)
     LSB_CUDA_OK(cudaMemsetAsync(dq_acc, 0, (size_t)align256(4 * B * H * N * D) + sizeof(int), st),
                 "attn_bwd dQ accumulator memset");
-  rc = bf ? launch_fa_bwd<1>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,
-                             causal, dtype, dsum, dq_acc, work_counter, st)
-          : launch_fa_bwd<0>(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale,
-                             causal, dtype, dsum, dq_acc, work_counter, st);
+  auto fa = bf ? (D == 128 ? launch_fa_bwd<1, 128> : launch_fa_bwd<1, 64>)
+               : (D == 128 ? launch_fa_bwd<0, 128> : launch_fa_bwd<0, 64>);
+  rc = fa(q, k, v, dout, lse, dk, dv, B, H, N, sq, sk, sv, sdo, sdk, sdv, scale, causal, dtype, dsum,
+          dq_acc, work_counter, st);
   if (rc) return rc;
   return bf ? launch_dq_cast<__nv_bfloat16>(dq_acc, dq, B, H, N, D, S4(sdq), st)
             : launch_dq_cast<__half>(dq_acc, dq, B, H, N, D, S4(sdq), st);

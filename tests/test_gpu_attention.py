@@ -99,7 +99,7 @@ def test_gradcheck(B, H, N, D, causal):
 
 
 BWD_SHAPES = [(1, 1, 17, 32), (2, 2, 64, 64), (1, 4, 130, 64), (2, 8, 256, 128), (1, 2, 300, 128),
-              (1, 2, 1000, 128)]
+              (1, 2, 1000, 128), (2, 4, 700, 64), (1, 20, 2048, 64)]
 
 
 @pytest.mark.parametrize("causal", [False, True])
@@ -117,12 +117,14 @@ def test_backward_matches_oracle(B, H, N, D, dtype, causal):
         torch.testing.assert_close(a.float().cpu(), e, atol=t, rtol=t, msg=n)
 
 
-def test_backward_simt_and_default_agree_bf16():
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_simt_and_default_agree_bf16(D):
+    """The tcgen05 backward (D = 64 and 128) against the SIMT kernel of the same library."""
     torch.manual_seed(3)
-    B, H, N, D = 1, 2, 256, 128
+    B, H, N = 1, 2, 256
     q, k, v, do = (torch.randn(B, H, N, D, device="cuda", dtype=torch.bfloat16) for _ in range(4))
     o, L = _flash_attention_forward_lse(q, k, v, True)
-    a = _flash_attention_backward(do, q, k, v, o, L, True)
+    a = _flash_attention_backward(do, q, k, v, o, L, True, impl=_lib.IMPL_TCGEN05)
     b = _flash_attention_backward(do, q, k, v, o, L, True, impl=_lib.IMPL_SIMT)
     for x, y in zip(a, b):
         torch.testing.assert_close(x.float(), y.float(), atol=3e-2, rtol=3e-2)
