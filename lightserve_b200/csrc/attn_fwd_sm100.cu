@@ -11,7 +11,9 @@
 // global counter in slice-group order (groups of BH_GROUP (batch, head)
 // slices; inside a group the longest causal items first), so the slices in
 // flight share K / V in L2 and every SM stays busy to the end.
-//  * warp 0: TMA producer and work fetcher. Q tiles per item (each tile as
+//  * warp 2: work fetcher: takes item ids from the counter and decodes them
+//    up to NIS items ahead into a shared-memory ring.
+//  * warp 0: TMA producer. Q tiles per item (each tile as
 //    soon as the previous item's last QK on it is done), K and V tiles of
 //    128 keys through a 2-stage ring that runs on across items.
 //  * warp 1: TMEM owner and single-thread MMA issuer. Two query tiles share
@@ -60,6 +62,12 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 #define LSB_FWD_GROUP 16
 #endif
 constexpr int BH_GROUP = LSB_FWD_GROUP;  // (batch, head) slices scheduled together
+// Variable-length mode with at most this many slice groups and sequences
+// enumerates only the items inside sequences (per-sequence block counts and
+// a per-group prefix table in shared memory); beyond it, items past a
+// sequence's end are fetched and skipped.
+constexpr int MAX_TABLE_GROUPS = 128;
+constexpr int MAX_TABLE_SEQS = 512;  // per-sequence block counts (uint16) in shared memory
 
 template <int D>
 struct Smem {
@@ -70,10 +78,12 @@ struct Smem {
   static constexpr int BAR_OFF = V_OFF + NS * KC * CHUNK_BYTES;
   // barriers: q_full[2], q_empty[2], k_full[NS], v_full[NS], kv_empty[NS], s_full[2],
   // p_full[2][2], pv_done[2], item_full[NIS], item_empty[NIS]
-  static constexpr int NBAR = 2 * TILES + 3 * NS + 4 * TILES + 2 * NIS;
+  static constexpr int NBAR = 2 * TILES + 3 * NS + 4 * TILES + 2 * NIS + 1;
   static constexpr int TMEM_SLOT_OFF = BAR_OFF + NBAR * 8;
   static constexpr int ITEM_OFF = TMEM_SLOT_OFF + 16;
-  static constexpr int BYTES = ITEM_OFF + NIS * 4;
+  static constexpr int TABLE_OFF = ITEM_OFF + NIS * 12;  // ids, then (slice, block) pairs
+  static constexpr int SEQ_NB_OFF = TABLE_OFF + (MAX_TABLE_GROUPS + 1) * 4;
+  static constexpr int BYTES = SEQ_NB_OFF + MAX_TABLE_SEQS * 2;
   static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
 };
 
@@ -90,6 +100,8 @@ struct Params {
   int num_q_ctas;
   float scale_log2;
   int causal;
+  int n_groups;  // ceil(BH / BH_GROUP)
+  int compact;   // variable-length mode: items from the shared-memory group table
 };
 
 // Work-item counters, one per in-flight launch (slot chosen per launch and
@@ -147,28 +159,14 @@ struct Item {
   int nkv_t[TILES];  // K/V tiles each query tile visits (0: tile past the end)
   int nkv;
 };
-__device__ __forceinline__ Item decode_item(int item, const Params& p) {
-  const int nq = p.num_q_ctas;
-  const int g = item / (BH_GROUP * nq);
-  const int rem = item - g * BH_GROUP * nq;
-  const int gsz = min(BH_GROUP, p.BH - g * BH_GROUP);
-  const int ci = rem / gsz;
-  Item w;
-  w.bh = g * BH_GROUP + rem % gsz;
-  w.b = w.bh / p.H;
-  w.h = w.bh % p.H;
-  const int c = p.causal ? (nq - 1 - ci) : ci;  // causal: longest items first
-  w.q0 = c * (TILES * BM);
-  if (p.cu_seqlens != nullptr) {
-    // Clamped to the tensor, so malformed offsets cannot reach outside it.
-    w.base = min(max(__ldg(p.cu_seqlens + w.b), 0), p.N);
-    w.n = min(max(__ldg(p.cu_seqlens + w.b + 1), w.base), p.N) - w.base;
-    w.tb = 0;
-  } else {
-    w.base = 0;
-    w.n = p.N;
-    w.tb = w.b;
-  }
+// Rows [base, base + n) of sequence b in variable-length mode, clamped to
+// the tensor so malformed offsets cannot reach outside it.
+__device__ __forceinline__ void seq_rows(const Params& p, int b, int& base, int& n) {
+  base = min(max(__ldg(p.cu_seqlens + b), 0), p.N);
+  n = min(max(__ldg(p.cu_seqlens + b + 1), base), p.N) - base;
+}
+
+__device__ __forceinline__ void finish_item(Item& w, const Params& p) {
   const int nkv_all = (w.n + BN - 1) / BN;
 #pragma unroll
   for (int t = 0; t < TILES; ++t) {
@@ -176,7 +174,86 @@ __device__ __forceinline__ Item decode_item(int item, const Params& p) {
     w.nkv_t[t] = qt0 >= w.n ? 0 : (p.causal ? min(nkv_all, qt0 / BN + 1) : nkv_all);
   }
   w.nkv = max(w.nkv_t[0], w.nkv_t[1]);
+}
+
+// The item of query block c (rows [256 c, 256 c + 256)) of slice bh.
+__device__ __forceinline__ Item make_item(const Params& p, int bh, int c) {
+  Item w;
+  w.bh = bh;
+  w.b = bh / p.H;
+  w.h = bh % p.H;
+  w.q0 = c * (TILES * BM);
+  if (p.cu_seqlens != nullptr) {
+    seq_rows(p, w.b, w.base, w.n);
+    w.tb = 0;
+  } else {
+    w.base = 0;
+    w.n = p.N;
+    w.tb = w.b;
+  }
+  finish_item(w, p);
   return w;
+}
+
+// Items are numbered group by group (BH_GROUP consecutive slices). Dense
+// mode: inside a group, block index major (causal: the longest blocks
+// first), slice minor. Compact variable-length mode (gtab = items before
+// each group): only blocks inside their sequence are numbered; inside a
+// group block index c descends and, at each c, the group's slices that
+// have a block c follow in slice order.
+__device__ __forceinline__ Item decode_item(int item, const Params& p, const int* gtab,
+                                            const uint16_t* seq_nb) {
+  if (p.compact) {
+    // Group: the last g with gtab[g] <= item (binary search).
+    int lo = 0, hi = p.n_groups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (gtab[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    const int g = lo;
+    const int r = item - gtab[g];
+    const int s0 = g * BH_GROUP;
+    const int gsz = min(BH_GROUP, p.BH - s0);
+    int nb[BH_GROUP];
+    int cmax = 0;
+    int sq = s0 / p.H, hh = s0 - sq * p.H;  // sequence and head of slice s0 + i
+#pragma unroll
+    for (int i = 0; i < BH_GROUP; ++i) {
+      nb[i] = i < gsz ? (int)seq_nb[sq] : 0;
+      cmax = max(cmax, nb[i] - 1);
+      if (++hh == p.H) { hh = 0; ++sq; }
+    }
+    // above(c) = items of the group at block indices > c (non-increasing in
+    // c); the item's block index is the smallest c with above(c) <= r.
+    auto above = [&](int c) {
+      int a = 0;
+#pragma unroll
+      for (int i = 0; i < BH_GROUP; ++i) a += max(0, nb[i] - 1 - c);
+      return a;
+    };
+    int clo = 0, chi = cmax;
+    while (clo < chi) {
+      const int mid = (clo + chi) >> 1;
+      if (above(mid) <= r) chi = mid; else clo = mid + 1;
+    }
+    const int c = clo;
+    int idx = r - above(c);  // position among the group's slices that have block c
+    int sel = 0;
+    for (int i = 0; i < gsz; ++i) {
+      if (nb[i] > c) {
+        if (idx == 0) { sel = i; break; }
+        --idx;
+      }
+    }
+    return make_item(p, s0 + sel, c);
+  }
+  const int nq = p.num_q_ctas;
+  const int g = item / (BH_GROUP * nq);
+  const int rem = item - g * BH_GROUP * nq;
+  const int gsz = min(BH_GROUP, p.BH - g * BH_GROUP);
+  const int ci = rem / gsz;
+  const int c = p.causal ? (nq - 1 - ci) : ci;  // causal: longest items first
+  return make_item(p, g * BH_GROUP + rem % gsz, c);
 }
 
 template <int D, int FMT>
@@ -199,18 +276,63 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   uint64_t* p_full = s_full + TILES;
   uint64_t* pv_done = p_full + 2 * TILES;      // [TILES]
   uint64_t* item_full = pv_done + TILES;       // [NIS]
-  uint64_t* item_empty = item_full + NIS;      // [NIS]: 9 arrivals (MMA, 8 softmax warps)
+  uint64_t* item_empty = item_full + NIS;      // [NIS]: 10 arrivals (TMA, MMA, 8 softmax warps)
+  // The TMA producer has reached the last K/V tiles of its current item: the
+  // fetcher may claim the next one.
+  uint64_t* fetch_go = item_empty + NIS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT_OFF);
   volatile int* item_ids = reinterpret_cast<volatile int*>(smem + L::ITEM_OFF);
+  // (slice, block) of each ring slot's item, decoded once by the producer.
+  volatile int* item_code = item_ids + NIS;
+  int* gtab = reinterpret_cast<int*>(smem + L::TABLE_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = p.BH * p.num_q_ctas;
+  uint16_t* seq_nb = reinterpret_cast<uint16_t*>(smem + L::SEQ_NB_OFF);
+  if (p.compact) {
+    // seq_nb[s] = 256-row blocks of sequence s (one load pair per thread);
+    // gtab[g] = items of the groups before g: per-group sums, then a prefix
+    // sum by warp 0 (shuffle scan over 32 groups at a time).
+    const int n_seqs = p.BH / p.H;
+    for (int sq = threadIdx.x; sq < n_seqs; sq += THREADS) {
+      int base, n;
+      seq_rows(p, sq, base, n);
+      // At most num_q_ctas blocks (max_seqlen rows), as in the uncompacted
+      // numbering.
+      seq_nb[sq] = (uint16_t)min((n + TILES * BM - 1) / (TILES * BM), p.num_q_ctas);
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < p.n_groups; g += THREADS) {
+      const int s0 = g * BH_GROUP, s1 = min(p.BH, s0 + BH_GROUP);
+      int cnt = 0;
+      for (int bh = s0; bh < s1; ++bh) cnt += seq_nb[bh / p.H];
+      gtab[g + 1] = cnt;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int carry = 0;
+      if (lane == 0) gtab[0] = 0;
+      for (int g0 = 0; g0 < p.n_groups; g0 += 32) {
+        const int g = g0 + lane;
+        int v = g < p.n_groups ? gtab[g + 1] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        if (g < p.n_groups) gtab[g + 1] = carry + v;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+    }
+    // The __syncthreads below (after TMEM allocation) publishes the table.
+  }
   // Consumer side of the work-item ring: id of the k-th item (>= n_items:
-  // no more work), or -1 when the wait gave up.
-  auto next_item = [&](int k) -> int {
+  // no more work), or -1 when the wait gave up; its slice and block index.
+  auto next_item = [&](int k, int& bh, int& c) -> int {
     const int slot = k % NIS;
     if (!mbar_wait(&item_full[slot], (k / NIS) & 1, 0x10A)) return -1;
     const int id = item_ids[slot];
+    bh = item_code[2 * slot];
+    c = item_code[2 * slot + 1];
     mbar_arrive(&item_empty[slot]);
     return id;
   };
@@ -231,8 +353,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     }
     for (int i = 0; i < NIS; ++i) {
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 9);
+      mbar_init(&item_empty[i], 10);
     }
+    mbar_init(fetch_go, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -243,6 +366,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int n_items = p.compact ? gtab[p.n_groups] : p.BH * p.num_q_ctas;
 
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sK = smem + L::K_OFF;
@@ -259,13 +383,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       int J = 0;  // running K/V tile count of this CTA
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int slot = k % NIS;
-        if (k >= NIS && !mbar_wait(&item_empty[slot], ((k / NIS) - 1) & 1, 0x104)) break;
-        const int item = atomicAdd(p.work_counter, 1);
-        item_ids[slot] = item;
-        mbar_arrive(&item_full[slot]);  // release: the id is visible to its waiters
-        if (item >= n_items) break;
-        const Item w = decode_item(item, p);
+        int ibh = 0, ic = 0;
+        const int item = next_item(k, ibh, ic);
+        if (item < 0 || item >= n_items) break;
+        const Item w = make_item(p, ibh, ic);
         for (int t = 0; t < TILES; ++t) {
           if (k > 0 && !mbar_wait(&q_empty[t], (k - 1) & 1, 0x103)) { ok = false; break; }
           if (w.nkv_t[t] == 0) {  // tile past the slice end: nothing to load
@@ -277,7 +398,15 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
             tma_load_4d(sQ + (t * KC + kc) * CHUNK_BYTES, &tq, &q_full[t], kc * 64,
                         w.base + w.q0 + t * BM, w.h, w.tb);
         }
+        // Claim point of the next item: four K/V tiles before the end of this
+        // one (its start for items of at most four tiles), close to the end
+        // of this item's compute, so the items left at the end of the
+        // launch stay unclaimed until an SM is about to need one, while the
+        // claim and its decoding still finish before the producer needs it.
+        const int go_at = max(w.nkv - 4, 0);
+        if (go_at == 0) mbar_arrive(fetch_go);
         for (int j = 0; ok && j < w.nkv; ++j, ++J) {
+          if (j == go_at && j > 0) mbar_arrive(fetch_go);
           const int s = J % NS;
           if (J >= NS && !mbar_wait(&kv_empty[s], ((J / NS) - 1) & 1, 0x101)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[s], KC * CHUNK_BYTES);
@@ -328,9 +457,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
       int jt[TILES] = {0, 0};        // running K/V step count per query tile
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int item = next_item(k);
+        int ibh = 0, ic = 0;
+        const int item = next_item(k, ibh, ic);
         if (item < 0 || item >= n_items) break;
-        const Item w = decode_item(item, p);
+        const Item w = make_item(p, ibh, ic);
         for (int t = 0; t < TILES && ok; ++t)
           if (!mbar_wait(&q_full[t], k & 1, 0x201)) ok = false;
         if (!ok) break;
@@ -367,8 +497,31 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         for (int t = 0; t < TILES; ++t) jt[t] += w.nkv_t[t];
       }
     }
+  } else if (warp == 2) {
+    // -------------------------------------------------------- work fetcher --
+    // Takes item ids from the global counter and decodes them into the ring,
+    // one item ahead of the TMA producer (claimed when the producer signals
+    // fetch_go), so neither the counter's latency nor the decoding sits on
+    // the producer's path.
+    reg_dealloc<96>();
+    if (lane == 0) {
+      for (int k = 0;; ++k) {
+        const int slot = k % NIS;
+        if (k >= NIS && !mbar_wait(&item_empty[slot], ((k / NIS) - 1) & 1, 0x104)) break;
+        if (k > 0 && !mbar_wait(fetch_go, (k - 1) & 1, 0x105)) break;
+        const int item = atomicAdd(p.work_counter, 1);
+        if (item < n_items) {
+          const Item w = decode_item(item, p, gtab, seq_nb);
+          item_code[2 * slot] = w.bh;
+          item_code[2 * slot + 1] = w.q0 / (TILES * BM);
+        }
+        item_ids[slot] = item;
+        mbar_arrive(&item_full[slot]);  // release: the item is visible to its waiters
+        if (item >= n_items) break;
+      }
+    }
   } else if (warp < 4) {
-    reg_dealloc<96>();  // warps 2-3: idle members of the TMA/MMA warpgroup
+    reg_dealloc<96>();  // warp 3: idle member of the TMA/MMA warpgroup
   } else {
     // ------------------------------------------------------------- softmax --
     reg_alloc<200>();
@@ -379,11 +532,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
     int jt = 0;  // running K/V step count of this query tile
     bool ok = true;
     for (int k = 0; ok; ++k) {
-      int item = 0;
-      if (lane == 0) item = next_item(k);
+      int item = 0, ibh = 0, ic = 0;
+      if (lane == 0) item = next_item(k, ibh, ic);
       item = __shfl_sync(0xffffffffu, item, 0);
+      ibh = __shfl_sync(0xffffffffu, ibh, 0);
+      ic = __shfl_sync(0xffffffffu, ic, 0);
       if (item < 0 || item >= n_items) break;
-      const Item w = decode_item(item, p);
+      const Item w = make_item(p, ibh, ic);
       const int nkv_t = w.nkv_t[t];
       const int qt0 = w.q0 + t * BM;
       const int row_g = qt0 + row;
@@ -553,6 +708,9 @@ static int launch_fa_fwd(const void* q, const void* k, const void* v, void* o, f
   p.BH = (int)((cu_seqlens != nullptr ? n_seqs : B) * H);
   const int64_t rows = cu_seqlens != nullptr ? max_seqlen : N;
   p.num_q_ctas = (int)((rows + TILES * BM - 1) / (TILES * BM));
+  p.n_groups = (p.BH + BH_GROUP - 1) / BH_GROUP;
+  p.compact = cu_seqlens != nullptr && p.n_groups <= MAX_TABLE_GROUPS && n_seqs <= MAX_TABLE_SEQS &&
+              rows <= (int64_t)TILES * BM * 0xffff;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal;
   // Work-item counter: a slot of g_work_counters per launch, zeroed in stream

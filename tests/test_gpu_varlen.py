@@ -134,3 +134,30 @@ def test_packed_prefill_matches_per_request_prefill():
     for a, b in zip(caches[0].k + caches[0].v, caches[1].k + caches[1].v):
         assert (a.float() - b.float()).norm() <= 2e-2 * b.float().norm()
     assert torch.equal(firsts[0], firsts[1])
+
+
+# Work numbering in variable-length mode: up to 128 groups of 16 (sequence,
+# head) slices and 512 sequences, only the 256-row blocks inside each
+# sequence are numbered (a table built in shared memory); above either
+# limit every slice gets max_seqlen / 256 blocks and those past its end are
+# skipped. Every item is computed the same way in both, so each sequence's
+# rows must equal the dense kernel's output for that sequence alone, bit for
+# bit.
+@pytest.mark.parametrize("lens,H,max_seqlen", [
+    ([4096, 1, 300, 0, 513, 256, 257, 2000, 17], 16, None),   # compact, many skipped blocks
+    ([513, 40, 1, 256], 4, 800),                              # max_seqlen above the longest
+    ([(37 * i) % 300 + 1 for i in range(130)], 16, None),     # 130 groups: uncompacted
+    ([(53 * i) % 200 + 1 for i in range(600)], 2, None),      # 600 sequences: uncompacted
+])
+def test_varlen_numbering_bit_identical_to_dense(lens, H, max_seqlen):
+    D = 128
+    q, k, v, cu = _pack(lens, H, D, torch.bfloat16, seed=len(lens) + H)
+    o = flash_attention_varlen(q, k, v, cu, max_seqlen or max(lens), causal=True)
+    for s, n in enumerate(lens):
+        if n == 0:
+            continue
+        a, b = int(cu[s]), int(cu[s + 1])
+        sl = lambda t: t[a:b].transpose(0, 1).unsqueeze(0)  # noqa: E731  [1, H, n, D]
+        dense = flash_attention_forward(sl(q).contiguous(), sl(k).contiguous(), sl(v).contiguous(),
+                                        causal=True)
+        assert torch.equal(sl(o), dense), f"sequence {s} (length {n})"
