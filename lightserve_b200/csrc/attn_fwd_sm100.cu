@@ -201,9 +201,9 @@ __device__ __forceinline__ Item make_item(const Params& p, int bh, int c) {
 // each group): only blocks inside their sequence are numbered; inside a
 // group block index c descends and, at each c, the group's slices that
 // have a block c follow in slice order.
-__device__ __forceinline__ Item decode_item(int item, const Params& p, const int* gtab,
-                                            const uint16_t* seq_nb) {
-  if (p.compact) {
+__device__ __forceinline__ Item decode_item(int item, const Params& p, bool compact,
+                                            const int* gtab, const uint16_t* seq_nb) {
+  if (compact) {
     // Group: the last g with gtab[g] <= item (binary search).
     int lo = 0, hi = p.n_groups - 1;
     while (lo < hi) {
@@ -366,7 +366,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_items = p.compact ? gtab[p.n_groups] : p.BH * p.num_q_ctas;
+  // The compact numbering pays for its longer decoding only when it drops
+  // more than an eighth of the items (every CTA decides alike).
+  const int n_all = p.BH * p.num_q_ctas;
+  const bool compact = p.compact && (int64_t)gtab[p.n_groups] * 8 < (int64_t)n_all * 7;
+  const int n_items = compact ? gtab[p.n_groups] : n_all;
 
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sK = smem + L::K_OFF;
@@ -511,7 +515,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CU
         if (k > 0 && !mbar_wait(fetch_go, (k - 1) & 1, 0x105)) break;
         const int item = atomicAdd(p.work_counter, 1);
         if (item < n_items) {
-          const Item w = decode_item(item, p, gtab, seq_nb);
+          const Item w = decode_item(item, p, compact, gtab, seq_nb);
           item_code[2 * slot] = w.bh;
           item_code[2 * slot + 1] = w.q0 / (TILES * BM);
         }
