@@ -149,9 +149,9 @@ def test_packed_prefill_matches_per_request_prefill():
     ([(37 * i) % 300 + 1 for i in range(130)], 16, None),     # 130 groups: uncompacted
     ([(53 * i) % 200 + 1 for i in range(600)], 2, None),      # 600 sequences: uncompacted
 ])
-def test_varlen_numbering_bit_identical_to_dense(lens, H, max_seqlen):
-    D = 128
-    q, k, v, cu = _pack(lens, H, D, torch.bfloat16, seed=len(lens) + H)
+@pytest.mark.parametrize("D,dtype", [(128, torch.bfloat16), (64, torch.float16)])
+def test_varlen_numbering_bit_identical_to_dense(lens, H, max_seqlen, D, dtype):
+    q, k, v, cu = _pack(lens, H, D, dtype, seed=len(lens) + H)
     o = flash_attention_varlen(q, k, v, cu, max_seqlen or max(lens), causal=True)
     for s, n in enumerate(lens):
         if n == 0:
